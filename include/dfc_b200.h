@@ -1,0 +1,202 @@
+/*
+ * dfc_b200.h -- C ABI of the B200 (sm_100a) DFC-AdamW step library
+ * (libdfc_b200.so).
+ *
+ * The reference (YellowJune/T3st) has no native layer: its optimizer step is
+ * eager PyTorch (remote/torch_fiber.py:68-117) and an unwired Triton kernel
+ * (remote/triton_dfc_adamw.py:24-101, one launch per tensor).  Each entry
+ * point below names the reference code it replaces.
+ *
+ * Conventions
+ *  - Every pointer inside a descriptor is a DEVICE pointer, except where a
+ *    comment says "host".  Descriptor arrays themselves (DfcSegment,
+ *    DfcHyper, DfcGradRef, DfcWordRange) are HOST arrays read during the call
+ *    and copied into the kernel's launch parameters: the caller may reuse
+ *    them as soon as the call returns.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *    is asynchronous and stream-ordered; none synchronises the host.
+ *  - Return value: DFC_OK (0) or a negative DFC_ERR_* code.  Nothing aborts,
+ *    nothing allocates device memory, nothing is cached between calls.
+ *  - Every launch is sized from its arguments; a bad argument is reported
+ *    before any launch (nothing is half-applied).
+ */
+#ifndef DFC_B200_H_
+#define DFC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFC_ABI_VERSION 1
+
+/* Entry points are the library's only exported symbols (it is built with
+ * -fvisibility=hidden). */
+#if defined(__GNUC__)
+#define DFC_API __attribute__((visibility("default")))
+#else
+#define DFC_API
+#endif
+
+/* ---- status codes ---- */
+#define DFC_OK 0
+#define DFC_ERR_NULL (-1)      /* required pointer is NULL */
+#define DFC_ERR_ALIGN (-2)     /* pointer not aligned to its element size */
+#define DFC_ERR_SIZE (-3)      /* negative, inconsistent or too large size */
+#define DFC_ERR_DTYPE (-4)     /* unknown gradient element type */
+#define DFC_ERR_MODE (-5)      /* unknown moment-word format */
+#define DFC_ERR_HYPER (-6)     /* hyper-set index out of range */
+#define DFC_ERR_CUDA (-7)      /* CUDA runtime error (see dfc_last_cuda_error) */
+#define DFC_ERR_RANGE (-8)     /* bit range outside the fiber */
+#define DFC_ERR_SCRATCH (-9)   /* scratch buffer too small */
+
+/* ---- moment-word formats ---- */
+/* FP32 moments, second moment used as stored (enable_fiber=False,
+ * remote/torch_fiber.py:94-96, 106-107). */
+#define DFC_MODE_PLAIN 0
+/* FP32 moments, bit 31 of the second-moment word is an opaque payload bit
+ * kept across the step (remote/torch_fiber.py:90-105). */
+#define DFC_MODE_SIGNFIBER 1
+/* Packed words: high 16 bits = moment rounded to the nearest bf16 (ties away
+ * from zero), low 16 bits = signed residual in FP32 ulps, so that
+ * fp32 = (hi << 16) + (int16)lo exactly.  Bit 31 of the first moment is its
+ * sign; bit 31 of the second moment is the payload bit. No counterpart in
+ * the reference (it stores FP32 moments). */
+#define DFC_MODE_PACKED 2
+
+/* ---- gradient element types ---- */
+#define DFC_GRAD_F32 0
+#define DFC_GRAD_BF16 1
+
+/* One contiguous run of elements updated by the step: a whole parameter, or
+ * the part of one that falls in a shard.  48 bytes. */
+typedef struct DfcSegment {
+  float* param;          /* FP32, updated in place */
+  const void* grad;      /* DFC_GRAD_F32 (float) or DFC_GRAD_BF16 (bf16 bits) */
+  uint32_t* exp_avg;     /* first-moment words, updated in place */
+  uint32_t* exp_avg_sq;  /* second-moment words, updated in place */
+  int64_t numel;
+  int32_t hyper;         /* index into the call's DfcHyper array */
+  int32_t grad_dtype;    /* DFC_GRAD_* */
+} DfcSegment;
+
+/* FP32 scalars of one (param group, step count) pair, each rounded once
+ * from the double the reference computes (remote/torch_fiber.py:75-116):
+ *   beta1, 1-beta1, beta2, 1-beta2, sqrt(1-beta2^step), eps,
+ *   decay = 1 - lr*wd (1 when wd == 0), neg_step_size = -lr/(1-beta1^step),
+ *   grad_scale multiplies the gradient first (1 = none).  48 bytes. */
+typedef struct DfcHyper {
+  float beta1;
+  float one_minus_beta1;
+  float beta2;
+  float one_minus_beta2;
+  float sqrt_bc2;
+  float eps;
+  float decay;
+  float neg_step_size;
+  float grad_scale;
+  float reserved[3];
+} DfcHyper;
+
+/* A gradient buffer for the statistics kernels.  24 bytes. */
+typedef struct DfcGradRef {
+  const void* grad;
+  int64_t numel;
+  int32_t grad_dtype;
+  int32_t reserved;
+} DfcGradRef;
+
+/* Per-buffer gradient statistics.  24 bytes. */
+typedef struct DfcGradStats {
+  double sumsq;        /* sum of g*g, accumulated in double */
+  float amax;          /* max |g| over non-NaN elements */
+  int32_t reserved;
+  int64_t nonfinite;   /* number of Inf/NaN elements */
+} DfcGradStats;
+
+/* A run of second-moment words whose bit 31 forms part of the sign fiber. */
+typedef struct DfcWordRange {
+  uint32_t* words;
+  int64_t count;
+} DfcWordRange;
+
+DFC_API int dfc_abi_version(void);
+DFC_API const char* dfc_strerror(int status);
+/* cudaError_t of the last DFC_ERR_CUDA returned on this host thread. */
+DFC_API int dfc_last_cuda_error(void);
+
+/*
+ * Fused multi-tensor DFC-AdamW step over `n_segments` segments in one launch
+ * (more launches only beyond the per-launch capacity, 560 segments or 32
+ * hyper sets).  Replaces the per-parameter loop of DFCAdamW.step
+ * (remote/torch_fiber.py:74-117) and the one-tensor Triton launcher
+ * dfc_adamw_step (remote/triton_dfc_adamw.py:63-101).
+ *
+ * segments, hypers: host arrays.  mode: DFC_MODE_*.  device_grad_scale:
+ * NULL, or a device float multiplied into every gradient after
+ * hyper.grad_scale (a clip coefficient computed on the device).
+ */
+DFC_API int dfc_mt_step(const DfcSegment* segments, int32_t n_segments, const DfcHyper* hypers,
+                int32_t n_hypers, int32_t mode, const float* device_grad_scale, void* stream);
+
+/*
+ * Convert moment words between the reference's FP32 layout and the packed
+ * layout, in place, over `n` words (no counterpart in the reference).
+ * second != 0: bit 31 is the payload bit and is kept.
+ * dfc_pack_moments: FP32 word -> packed word; dfc_unpack_moments: inverse.
+ */
+DFC_API int dfc_pack_moments(uint32_t* words, int64_t n, int32_t second, void* stream);
+DFC_API int dfc_unpack_moments(uint32_t* words, int64_t n, int32_t second, void* stream);
+
+/*
+ * bf16 gradient compression with per-element error feedback over a flat
+ * buffer (no counterpart in the reference, which keeps FP32 gradients,
+ * remote/torch_fiber.py:83).  s = grad + e, where e is the residual left by
+ * the previous call and recovered exactly from (comp, resid); comp <- s
+ * rounded to the nearest bf16 (ties away from zero); resid <- the signed
+ * 16-bit residual field.  comp and resid are read and written in place;
+ * both start at zero.
+ */
+DFC_API int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resid, int64_t n, void* stream);
+
+/*
+ * Per-buffer gradient statistics with warp-shuffle block reductions and a
+ * fixed-order second pass (deterministic).  `out` receives n_grads records
+ * (device).  `scratch` (device) must hold dfc_grad_stats_scratch_bytes()
+ * bytes.  No counterpart in the reference (it computes no statistics).
+ */
+DFC_API size_t dfc_grad_stats_scratch_bytes(const DfcGradRef* grads, int32_t n_grads);
+DFC_API int dfc_grad_stats(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* out, void* scratch,
+                   size_t scratch_bytes, void* stream);
+
+/*
+ * Global-norm clip coefficient from statistics records, on the device:
+ * total = sqrt(sum sumsq); coef = min(1, max_norm / (total + 1e-6)).
+ * Writes the coefficient to out_coef[0] and the norm to out_norm[0] (either
+ * may be NULL).  Feeds dfc_mt_step's device_grad_scale.
+ */
+DFC_API int dfc_clip_coef(const DfcGradStats* stats, int32_t n_stats, float max_norm, float* out_coef,
+                  float* out_norm, void* stream);
+
+/*
+ * Sign-fiber payload I/O on the device.  The fiber is the concatenation of
+ * bit 31 of every word of the ranges, in order (remote/torch_fiber.py:
+ * 120-185, TorchSignFiberChannel).  Bits [start_bit, start_bit + n_bits)
+ * are read into / written from `bytes` (device, ceil(n_bits/8) bytes),
+ * packed 8 per byte, least-significant bit first
+ * (np.packbits(bitorder="little"), remote/torch_fiber.py:178, 184).  A read
+ * leaves the unused high bits of the last byte zero; a write consumes
+ * exactly n_bits bits.  Only bit 31 of each word is touched.
+ */
+DFC_API int dfc_fiber_read(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
+                   int64_t n_bits, uint8_t* bytes, void* stream);
+DFC_API int dfc_fiber_write(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
+                    int64_t n_bits, const uint8_t* bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DFC_B200_H_ */

@@ -1,0 +1,216 @@
+/*
+ * CPU oracle for the DFC-AdamW step.  TEST INFRASTRUCTURE ONLY: the parity
+ * tests, the smoke check and the CPU-baseline leg of the benchmark call this
+ * to check (or time beside) the CUDA path; the product never links it.
+ *
+ * It restates, element by element and in plain C with explicit rounding, the
+ * arithmetic of the reference's eager-PyTorch optimizer step
+ * (remote/torch_fiber.py:68-117, YellowJune/T3st):
+ *
+ *   m1  = m * f32(beta1)                          torch_fiber.py:98  mul_(beta1)
+ *   m'  = fma(g, f32(1 - beta1), m1)              torch_fiber.py:98  add_(g, alpha=1-beta1)
+ *   v1  = v * f32(beta2)                          torch_fiber.py:99  mul_(beta2)
+ *   v'  = fma(f32(1 - beta2) * g, g, v1)          torch_fiber.py:99  addcmul_(g, g, value=1-beta2)
+ *   den = sqrt(v') / f32(sqrt(bc2)) + f32(eps)    torch_fiber.py:112
+ *   p1  = p * f32(1 - lr * wd)                    torch_fiber.py:114-115
+ *   p'  = p1 + (f32(-lr / bc1) * m') / den        torch_fiber.py:116 addcdiv_
+ *
+ * All scalars are formed in double on the host and rounded once to f32, as
+ * PyTorch does when a Python float meets an FP32 tensor.  The sign-fiber mode
+ * strips bit 31 of the second-moment word before the update and puts it back
+ * afterwards (torch_fiber.py:18-19, 90-107).
+ *
+ * Two formats have no counterpart in the reference and are specified here:
+ *
+ * Packed moment word (bf16 high half + 16-bit error-feedback residual low
+ * half).  For an FP32 magnitude a (31 bits):
+ *     enc(a) = a + ((a & 0x8000) << 1)        for a <= 0x7F800000
+ *     enc(a) = a | 0x00400000                 for NaN
+ * so the high half is a rounded to the nearest bf16 (ties away from zero) and
+ * the low half, read as a signed int16, is the residual in units of the FP32
+ * ulp: dec(W) = (hi << 16) + (int16)lo, clamped to [0, 0x7F800000] (NaN words,
+ * hi > 0x7F80, decode to themselves).  Every 16-bit residual pattern is a
+ * valid residual, and dec(enc(a)) == a for every FP32 value except that NaNs
+ * come back quiet.  The first moment keeps its sign in bit 31; the second
+ * moment keeps the reference's payload bit in bit 31 and its magnitude in the
+ * rest.
+ *
+ * Compressed gradient with error feedback.  s = g + e, c = high half of
+ * enc(s) (bf16, contiguous for the collective), q = low half (the residual
+ * field).  The next call recovers e = dec(c, q) - c exactly; e is 0 when c is
+ * not finite.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define ORC_MODE_PLAIN 0
+#define ORC_MODE_SIGNFIBER 1
+#define ORC_MODE_PACKED 2
+
+typedef struct orc_hyper {
+  float beta1;
+  float one_minus_beta1;
+  float beta2;
+  float one_minus_beta2;
+  float sqrt_bc2;
+  float eps;
+  float decay;
+  float neg_step_size;
+  float grad_scale;
+} orc_hyper;
+
+static inline uint32_t f2u(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  return u;
+}
+static inline float u2f(uint32_t u) {
+  float x;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+/* ---- packed word: magnitude encode/decode (31-bit values) ---- */
+uint32_t orc_enc_mag(uint32_t a) {
+  if (a > 0x7F800000u) return a | 0x00400000u;
+  return a + ((a & 0x8000u) << 1);
+}
+
+uint32_t orc_dec_mag(uint32_t w) {
+  uint32_t hi = w >> 16;
+  if (hi > 0x7F80u) return w;
+  int32_t r = (int32_t)(hi << 16) + (int32_t)(int16_t)(w & 0xFFFFu);
+  if (r < 0) r = 0;
+  if (r > 0x7F800000) r = 0x7F800000;
+  return (uint32_t)r;
+}
+
+uint32_t orc_pack_signed(float x) {
+  uint32_t b = f2u(x);
+  return (b & 0x80000000u) | orc_enc_mag(b & 0x7FFFFFFFu);
+}
+
+float orc_unpack_signed(uint32_t w) {
+  return u2f((w & 0x80000000u) | orc_dec_mag(w & 0x7FFFFFFFu));
+}
+
+static inline float bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* ---- one element of the step ---- */
+static inline void step_one(int mode, const orc_hyper* h, float* p, float gin, uint32_t* mw,
+                            uint32_t* vw) {
+  float g = gin * h->grad_scale;
+  float m, v;
+  uint32_t payload = 0;
+  if (mode == ORC_MODE_PACKED) {
+    m = orc_unpack_signed(*mw);
+    payload = *vw & 0x80000000u;
+    v = u2f(orc_dec_mag(*vw & 0x7FFFFFFFu));
+  } else if (mode == ORC_MODE_SIGNFIBER) {
+    m = u2f(*mw);
+    payload = *vw & 0x80000000u;
+    v = u2f(*vw & 0x7FFFFFFFu);
+  } else {
+    m = u2f(*mw);
+    v = u2f(*vw);
+  }
+  float m1 = m * h->beta1;
+  float m_new = fmaf(g, h->one_minus_beta1, m1);
+  float v1 = v * h->beta2;
+  float t = h->one_minus_beta2 * g;
+  float v_new = fmaf(t, g, v1);
+
+  uint32_t v_store;
+  float v_upd;
+  if (mode == ORC_MODE_PLAIN) {
+    v_store = f2u(v_new);
+    v_upd = v_new;
+  } else {
+    uint32_t mag = f2u(v_new) & 0x7FFFFFFFu;
+    v_upd = u2f(mag);
+    v_store = payload | (mode == ORC_MODE_PACKED ? orc_enc_mag(mag) : mag);
+  }
+  float den = sqrtf(v_upd) / h->sqrt_bc2 + h->eps;
+  float p1 = *p * h->decay;
+  float upd = (h->neg_step_size * m_new) / den;
+  *p = p1 + upd;
+  *mw = (mode == ORC_MODE_PACKED) ? orc_pack_signed(m_new) : f2u(m_new);
+  *vw = v_store;
+}
+
+int orc_step_f32(int mode, const orc_hyper* h, float* p, const float* g, uint32_t* m, uint32_t* v,
+                 int64_t n) {
+  if (mode < 0 || mode > 2) return -1;
+  for (int64_t i = 0; i < n; ++i) step_one(mode, h, p + i, g[i], m + i, v + i);
+  return 0;
+}
+
+int orc_step_bf16(int mode, const orc_hyper* h, float* p, const uint16_t* g, uint32_t* m,
+                  uint32_t* v, int64_t n) {
+  if (mode < 0 || mode > 2) return -1;
+  for (int64_t i = 0; i < n; ++i) step_one(mode, h, p + i, bf16_to_f32(g[i]), m + i, v + i);
+  return 0;
+}
+
+/* ---- packed-word array conversions ---- */
+void orc_pack_first(const float* x, uint32_t* w, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) w[i] = orc_pack_signed(x[i]);
+}
+void orc_unpack_first(const uint32_t* w, float* x, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) x[i] = orc_unpack_signed(w[i]);
+}
+/* second moment: bit 31 of the input FP32 word is the payload and is kept */
+void orc_pack_second(const uint32_t* physical, uint32_t* w, int64_t n) {
+  for (int64_t i = 0; i < n; ++i)
+    w[i] = (physical[i] & 0x80000000u) | orc_enc_mag(physical[i] & 0x7FFFFFFFu);
+}
+void orc_unpack_second(const uint32_t* w, uint32_t* physical, int64_t n) {
+  for (int64_t i = 0; i < n; ++i)
+    physical[i] = (w[i] & 0x80000000u) | orc_dec_mag(w[i] & 0x7FFFFFFFu);
+}
+
+/* ---- compressed gradient with error feedback ---- */
+static inline float ef_residual(uint16_t c, uint16_t q) {
+  uint32_t hm = c & 0x7FFFu;
+  if (hm >= 0x7F80u) return 0.0f;
+  uint32_t sign = ((uint32_t)c & 0x8000u) << 16;
+  float s = u2f(sign | orc_dec_mag((hm << 16) | q));
+  return s - bf16_to_f32(c);
+}
+
+void orc_compress_ef(const float* g, uint16_t* c, uint16_t* q, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float s = g[i] + ef_residual(c[i], q[i]);
+    uint32_t b = f2u(s);
+    uint32_t w = (b & 0x80000000u) | orc_enc_mag(b & 0x7FFFFFFFu);
+    c[i] = (uint16_t)(w >> 16);
+    q[i] = (uint16_t)(w & 0xFFFFu);
+  }
+}
+
+/* value the residual field carries, for inspection */
+void orc_ef_residual(const uint16_t* c, const uint16_t* q, float* e, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) e[i] = ef_residual(c[i], q[i]);
+}
+
+/* ---- per-tensor gradient statistics ---- */
+void orc_grad_stats(const float* g, int64_t n, double* sumsq, float* amax, int64_t* nonfinite) {
+  double s = 0.0;
+  float a = 0.0f;
+  int64_t bad = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    float x = g[i];
+    s += (double)x * (double)x;
+    a = fmaxf(a, fabsf(x));
+    if (!isfinite(x)) ++bad;
+  }
+  *sumsq = s;
+  *amax = a;
+  *nonfinite = bad;
+}
+
+/* ---- sign-fiber bit I/O over a list of second-moment tensors ---- */
+void orc_fiber_read_bits(const uint32_t* words, int64_t n, uint8_t* bits) {
+  for (int64_t i = 0; i < n; ++i) bits[i] = (uint8_t)(words[i] >> 31);
+}

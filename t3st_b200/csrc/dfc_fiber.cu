@@ -1,0 +1,135 @@
+// Sign-fiber payload I/O on the device: bit 31 of every second-moment word,
+// concatenated over a list of word ranges, read into or written from a
+// little-endian packed byte buffer (remote/torch_fiber.py:120-185).  One
+// thread per payload byte; it owns the 8 words behind that byte, so writes
+// never race and a read is one pass.  The range list lives in launch
+// parameters (up to kMaxRanges per launch); a call with more ranges is split
+// into launches at byte boundaries of the payload.
+#include <algorithm>
+
+#include "dfc_common.cuh"
+
+namespace dfc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxRanges = 1300;
+
+struct FiberBatch {
+  int32_t n_ranges;
+  int32_t pad;
+  int64_t first_bit;   // global fiber bit of this launch's byte 0 (byte aligned in the payload)
+  int64_t n_bits;      // bits this launch reads/writes, starting at first_bit
+  int64_t range_base[kMaxRanges + 1];  // global fiber bit of each range's word 0
+  uint32_t* words[kMaxRanges];
+};
+static_assert(sizeof(FiberBatch) <= 32000, "launch parameter limit");
+
+__device__ __forceinline__ int find_range(const FiberBatch& b, int64_t g) {
+  int lo = 0, hi = b.n_ranges;  // range_base[lo] <= g < range_base[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.range_base[mid] <= g) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+template <bool WRITE>
+__global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__ FiberBatch b,
+                                                         uint8_t* bytes) {
+  const int64_t nbytes = (b.n_bits + 7) / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t k = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; k < nbytes;
+       k += stride) {
+    const int nb = static_cast<int>(min(static_cast<int64_t>(8), b.n_bits - 8 * k));
+    int64_t g = b.first_bit + 8 * k;
+    int r = find_range(b, g);
+    uint32_t in = WRITE ? bytes[k] : 0u;
+    uint32_t out = 0u;
+    for (int j = 0; j < nb; ++j, ++g) {
+      while (g >= b.range_base[r + 1]) ++r;
+      uint32_t* w = b.words[r] + (g - b.range_base[r]);
+      if (WRITE) {
+        *w = (*w & 0x7FFFFFFFu) | (((in >> j) & 1u) << 31);
+      } else {
+        out |= (*w >> 31) << j;
+      }
+    }
+    if (!WRITE) bytes[k] = static_cast<uint8_t>(out);
+  }
+}
+
+template <bool WRITE>
+int fiber_call(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit, int64_t n_bits,
+               uint8_t* bytes, cudaStream_t st) {
+  if (n_ranges < 0 || start_bit < 0 || n_bits < 0) return n_ranges < 0 ? DFC_ERR_SIZE : DFC_ERR_RANGE;
+  if (n_ranges > 0 && !ranges) return DFC_ERR_NULL;
+  int64_t total = 0;
+  for (int32_t i = 0; i < n_ranges; ++i) {
+    if (ranges[i].count < 0) return DFC_ERR_SIZE;
+    if (ranges[i].count > 0 && !ranges[i].words) return DFC_ERR_NULL;
+    if (!aligned(ranges[i].words, 4)) return DFC_ERR_ALIGN;
+    total += ranges[i].count;
+  }
+  if (start_bit > total || n_bits > total - start_bit) return DFC_ERR_RANGE;
+  if (n_bits == 0) return DFC_OK;
+  if (!bytes) return DFC_ERR_NULL;
+
+  // Walk the ranges that intersect [start_bit, start_bit + n_bits) and cut
+  // the payload into launches of at most kMaxRanges ranges, each starting on
+  // a payload byte boundary so no two launches share a byte.
+  FiberBatch b;
+  int64_t pos = 0;        // global bit of range i's first word
+  int32_t i = 0;
+  while (i < n_ranges && pos + ranges[i].count <= start_bit) pos += ranges[i++].count;
+  int64_t done = 0;       // payload bits handled so far
+  while (done < n_bits) {
+    const int64_t first = start_bit + done;
+    // rewind to the range holding `first`
+    while (pos + ranges[i].count <= first) pos += ranges[i++].count;
+    b.n_ranges = 0;
+    b.first_bit = first;
+    int64_t p = pos;
+    int32_t j = i;
+    while (j < n_ranges && b.n_ranges < kMaxRanges && p < start_bit + n_bits) {
+      if (ranges[j].count > 0) {
+        b.range_base[b.n_ranges] = p;
+        b.words[b.n_ranges] = ranges[j].words;
+        ++b.n_ranges;
+      }
+      p += ranges[j].count;
+      ++j;
+    }
+    b.range_base[b.n_ranges] = p;
+    int64_t end = std::min<int64_t>(p, start_bit + n_bits);
+    if (end < start_bit + n_bits) {
+      // not the last launch: stop at the last whole payload byte
+      const int64_t whole = ((end - first) / 8) * 8;
+      end = first + whole;
+      if (whole == 0) return DFC_ERR_SIZE;  // more than kMaxRanges ranges inside one byte
+    }
+    b.n_bits = end - first;
+    const int64_t nbytes = (b.n_bits + 7) / 8;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nbytes + kThreads - 1) / kThreads, 148 * 8)));
+    fiber_kernel<WRITE><<<grid, kThreads, 0, st>>>(b, bytes + done / 8);
+    const int rc = launch_status();
+    if (rc != DFC_OK) return rc;
+    done += b.n_bits;
+  }
+  return DFC_OK;
+}
+
+}  // namespace
+}  // namespace dfc
+
+extern "C" int dfc_fiber_read(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
+                              int64_t n_bits, uint8_t* bytes, void* stream) {
+  return dfc::fiber_call<false>(ranges, n_ranges, start_bit, n_bits, bytes,
+                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dfc_fiber_write(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
+                               int64_t n_bits, const uint8_t* bytes, void* stream) {
+  return dfc::fiber_call<true>(ranges, n_ranges, start_bit, n_bits, const_cast<uint8_t*>(bytes),
+                               static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,264 @@
+// Per-buffer gradient statistics (sum of squares, max |g|, non-finite count)
+// and the global-norm clip coefficient.
+//
+// Pass 1: one CTA per tile of kTile elements of one buffer; each thread
+// accumulates its elements (sum of squares in double), then the CTA reduces
+// with warp shuffles (__shfl_xor_sync butterfly) and one shared-memory step
+// across warps, and writes one partial record per tile to scratch.
+// Pass 2: one warp per buffer folds that buffer's partial records in a fixed
+// order.  No atomics anywhere, so the result depends only on the input and
+// the tile size, never on scheduling.
+#include <algorithm>
+#include <math.h>
+
+#include "dfc_common.cuh"
+
+namespace dfc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTile = 8192;
+constexpr int kMaxBufs = 1000;
+
+struct BufArg {
+  const void* g;
+  int64_t n;
+  int32_t bf16;
+  int32_t vec;
+};
+
+struct StatsBatch {
+  DfcGradStats* partial;  // scratch, one record per tile of this batch
+  DfcGradStats* out;      // one record per buffer of this batch
+  int32_t n_bufs;
+  int32_t tile_base[kMaxBufs + 1];
+  BufArg buf[kMaxBufs];
+};
+static_assert(sizeof(StatsBatch) <= 32000, "launch parameter limit");
+
+struct Acc {
+  double s;
+  float a;
+  long long bad;
+};
+
+__device__ __forceinline__ void acc_add(Acc& acc, float x) {
+  acc.s += static_cast<double>(x) * static_cast<double>(x);
+  acc.a = fmaxf(acc.a, fabsf(x));
+  acc.bad += isfinite(x) ? 0 : 1;
+}
+
+__device__ __forceinline__ void acc_merge(Acc& acc, const Acc& o) {
+  acc.s += o.s;
+  acc.a = fmaxf(acc.a, o.a);
+  acc.bad += o.bad;
+}
+
+__device__ __forceinline__ Acc warp_fold(Acc acc) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    Acc o;
+    o.s = __shfl_xor_sync(0xFFFFFFFFu, acc.s, off);
+    o.a = __shfl_xor_sync(0xFFFFFFFFu, acc.a, off);
+    o.bad = __shfl_xor_sync(0xFFFFFFFFu, acc.bad, off);
+    acc_merge(acc, o);
+  }
+  return acc;
+}
+
+__device__ __forceinline__ float load1(const BufArg& b, int64_t i) {
+  return b.bf16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(b.g)[i])
+                : static_cast<const float*>(b.g)[i];
+}
+
+__global__ void __launch_bounds__(kThreads) stats_partial_kernel(const __grid_constant__ StatsBatch b) {
+  const int32_t t = static_cast<int32_t>(blockIdx.x);
+  int lo = 0, hi = b.n_bufs;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
+  }
+  const BufArg& buf = b.buf[lo];
+  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+  const int64_t count = min(static_cast<int64_t>(kTile), buf.n - base);
+
+  Acc acc{0.0, 0.0f, 0};
+  int64_t done = 0;
+  if (buf.vec && !buf.bf16) {
+    const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(buf.g) + base);
+    const int64_t nv = count / 4;
+    for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
+      const float4 x = __ldcs(g4 + j);
+      acc_add(acc, x.x);
+      acc_add(acc, x.y);
+      acc_add(acc, x.z);
+      acc_add(acc, x.w);
+    }
+    done = nv * 4;
+  }
+  for (int64_t j = done + threadIdx.x; j < count; j += kThreads) acc_add(acc, load1(buf, base + j));
+
+  acc = warp_fold(acc);
+  __shared__ Acc part[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) part[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Acc tot = part[0];
+    for (int w = 1; w < kWarps; ++w) acc_merge(tot, part[w]);
+    DfcGradStats r;
+    r.sumsq = tot.s;
+    r.amax = tot.a;
+    r.reserved = 0;
+    r.nonfinite = tot.bad;
+    b.partial[t] = r;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) stats_final_kernel(const __grid_constant__ StatsBatch b) {
+  const int warp_global = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= b.n_bufs) return;
+  const int32_t t0 = b.tile_base[warp_global], t1 = b.tile_base[warp_global + 1];
+  Acc acc{0.0, 0.0f, 0};
+  for (int32_t t = t0 + lane; t < t1; t += 32) {
+    const DfcGradStats r = b.partial[t];
+    Acc o{r.sumsq, r.amax, r.nonfinite};
+    acc_merge(acc, o);
+  }
+  acc = warp_fold(acc);
+  if (lane == 0) {
+    DfcGradStats r;
+    r.sumsq = acc.s;
+    r.amax = acc.a;
+    r.reserved = 0;
+    r.nonfinite = acc.bad;
+    b.out[warp_global] = r;
+  }
+}
+
+int64_t tiles_of(int64_t n) { return (n + kTile - 1) / kTile; }
+
+int validate(const DfcGradRef& r) {
+  if (r.numel < 0) return DFC_ERR_SIZE;
+  if (r.grad_dtype != DFC_GRAD_F32 && r.grad_dtype != DFC_GRAD_BF16) return DFC_ERR_DTYPE;
+  if (r.numel == 0) return DFC_OK;
+  if (!r.grad) return DFC_ERR_NULL;
+  if (!aligned(r.grad, r.grad_dtype == DFC_GRAD_BF16 ? 2 : 4)) return DFC_ERR_ALIGN;
+  if (tiles_of(r.numel) > INT32_MAX / 2) return DFC_ERR_SIZE;
+  return DFC_OK;
+}
+
+}  // namespace
+
+// Shared with the scratch-free variant: launches both passes over `grads`,
+// with partial records at `partial` (n_tiles_total records).
+int grad_stats_launch(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* out,
+                      DfcGradStats* partial, cudaStream_t st) {
+  StatsBatch b;
+  int64_t tile_off = 0;
+  int32_t first = 0;
+  while (first < n_grads) {
+    b.partial = partial + tile_off;
+    b.out = out + first;
+    b.n_bufs = 0;
+    b.tile_base[0] = 0;
+    int32_t i = first;
+    // Every buffer gets a record, so empty buffers take one (empty) tile.
+    while (i < n_grads && b.n_bufs < kMaxBufs) {
+      const int64_t tl = std::max<int64_t>(1, tiles_of(grads[i].numel));
+      if (b.tile_base[b.n_bufs] + tl > INT32_MAX / 2 && b.n_bufs > 0) break;
+      BufArg a;
+      a.g = grads[i].grad;
+      a.n = grads[i].numel;
+      a.bf16 = grads[i].grad_dtype == DFC_GRAD_BF16;
+      a.vec = aligned(grads[i].grad, 16);
+      b.buf[b.n_bufs] = a;
+      b.tile_base[b.n_bufs + 1] = b.tile_base[b.n_bufs] + static_cast<int32_t>(tl);
+      ++b.n_bufs;
+      ++i;
+    }
+    const int32_t tiles = b.tile_base[b.n_bufs];
+    stats_partial_kernel<<<tiles, kThreads, 0, st>>>(b);
+    const int warps_per_block = kThreads / 32;
+    stats_final_kernel<<<(b.n_bufs + warps_per_block - 1) / warps_per_block, kThreads, 0, st>>>(b);
+    const int rc = launch_status();
+    if (rc != DFC_OK) return rc;
+    tile_off += tiles;
+    first = i;
+  }
+  return DFC_OK;
+}
+
+size_t grad_stats_records(const DfcGradRef* grads, int32_t n_grads) {
+  size_t total = 0;
+  for (int32_t i = 0; i < n_grads; ++i)
+    total += static_cast<size_t>(std::max<int64_t>(1, tiles_of(std::max<int64_t>(0, grads[i].numel))));
+  return total;
+}
+
+int grad_stats_validate(const DfcGradRef* grads, int32_t n_grads) {
+  if (n_grads < 0) return DFC_ERR_SIZE;
+  if (n_grads > 0 && !grads) return DFC_ERR_NULL;
+  for (int32_t i = 0; i < n_grads; ++i) {
+    const int rc = validate(grads[i]);
+    if (rc != DFC_OK) return rc;
+  }
+  return DFC_OK;
+}
+
+namespace {
+
+__global__ void __launch_bounds__(kThreads)
+    clip_kernel(const DfcGradStats* stats, int32_t n, float max_norm, float* coef, float* norm) {
+  double s = 0.0;
+  for (int32_t i = threadIdx.x; i < n; i += kThreads) s += stats[i].sumsq;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
+  __shared__ double part[kWarps];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = part[0];
+    for (int w = 1; w < kWarps; ++w) tot += part[w];
+    const float total = static_cast<float>(sqrt(tot));
+    const float c = fminf(__fdiv_rn(max_norm, __fadd_rn(total, 1e-6f)), 1.0f);
+    if (coef) *coef = c;
+    if (norm) *norm = total;
+  }
+}
+
+}  // namespace
+}  // namespace dfc
+
+extern "C" size_t dfc_grad_stats_scratch_bytes(const DfcGradRef* grads, int32_t n_grads) {
+  if (n_grads <= 0 || !grads) return 0;
+  return dfc::grad_stats_records(grads, n_grads) * sizeof(DfcGradStats);
+}
+
+extern "C" int dfc_grad_stats(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* out,
+                              void* scratch, size_t scratch_bytes, void* stream) {
+  using namespace dfc;
+  int rc = grad_stats_validate(grads, n_grads);
+  if (rc != DFC_OK) return rc;
+  if (n_grads == 0) return DFC_OK;
+  if (!out || !scratch) return DFC_ERR_NULL;
+  if (!aligned(out, 8) || !aligned(scratch, 8)) return DFC_ERR_ALIGN;
+  if (scratch_bytes < grad_stats_records(grads, n_grads) * sizeof(DfcGradStats))
+    return DFC_ERR_SCRATCH;
+  return grad_stats_launch(grads, n_grads, out, static_cast<DfcGradStats*>(scratch),
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dfc_clip_coef(const DfcGradStats* stats, int32_t n_stats, float max_norm,
+                             float* out_coef, float* out_norm, void* stream) {
+  using namespace dfc;
+  if (n_stats < 0) return DFC_ERR_SIZE;
+  if (!stats && n_stats > 0) return DFC_ERR_NULL;
+  if (!out_coef && !out_norm) return DFC_OK;
+  if (!aligned(stats, 8) || !aligned(out_coef, 4) || !aligned(out_norm, 4)) return DFC_ERR_ALIGN;
+  clip_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(stats, n_stats, max_norm,
+                                                                      out_coef, out_norm);
+  return launch_status();
+}

@@ -1,0 +1,361 @@
+// Fused multi-tensor DFC-AdamW step for sm_100a.
+//
+// One launch updates every segment (parameter, or part of one) of the call.
+// The segment list, the per-segment tile prefix and the hyper sets travel in
+// the kernel's launch parameters (__grid_constant__, read through the
+// constant cache), so a step needs no device-side descriptor table, no
+// host->device copy and no allocation.  Each CTA owns one tile of kTile
+// consecutive elements of one segment and finds its segment by binary search
+// over the tile prefix.  A full, 16-byte-aligned tile is moved with 128-bit
+// streaming loads/stores (ld.global.cs / st.global.cs: every byte is touched
+// once per step), all kUnroll loads of the four streams issued before any
+// arithmetic so each thread keeps 4*kUnroll 16-byte requests in flight.
+//
+// Element arithmetic restates remote/torch_fiber.py:90-116 with explicit
+// rounding (no contraction: -fmad=false and __f*_rn intrinsics):
+//   g   = (g * grad_scale) * device_scale
+//   m'  = fma(g, 1-b1, m*b1)            :98   mul_ then add_(alpha)
+//   v'  = fma((1-b2)*g, g, v*b2)        :99   mul_ then addcmul_
+//   den = sqrt(v')/sqrt(bc2) + eps      :112  IEEE sqrt and divide
+//   p'  = p*decay + (-lr/bc1 * m')/den  :114-116 mul_, addcdiv_
+// Sign fiber (:90-107): bit 31 of v is masked off before and restored after.
+// Packed words: decoded before and re-encoded after with integer bit ops.
+
+#include <algorithm>
+#include <vector>
+
+#include "dfc_common.cuh"
+
+namespace dfc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kVec = 4;
+constexpr int kUnroll = 4;
+constexpr int kTile = kThreads * kVec * kUnroll;  // 4096 elements per CTA
+
+constexpr int32_t kFlagBf16 = 1;
+constexpr int32_t kFlagVec = 2;
+
+struct SegArg {
+  float* p;
+  const void* g;
+  uint32_t* m;
+  uint32_t* v;
+  int64_t n;
+  int32_t hyper;
+  int32_t flags;
+};
+static_assert(sizeof(SegArg) == 48, "SegArg layout");
+
+template <int MAXS, int MAXH>
+struct StepBatch {
+  const float* dev_scale;
+  int32_t n_segs;
+  int32_t tile_base[MAXS + 1];  // tile_base[i] = first tile of segment i
+  DfcHyper hyper[MAXH];
+  SegArg seg[MAXS];
+};
+
+constexpr int kSmallSegs = 64, kSmallHypers = 8;
+constexpr int kLargeSegs = 560, kLargeHypers = 32;
+static_assert(sizeof(StepBatch<kLargeSegs, kLargeHypers>) <= 32000, "launch parameter limit");
+
+struct Scalars {
+  float b1, omb1, b2, omb2, sbc2, eps, decay, nstep, gscale, dscale;
+};
+
+template <int MODE>
+__device__ __forceinline__ void step_elem(const Scalars& s, float& p, float gin, uint32_t& mw,
+                                          uint32_t& vw) {
+  const float g = __fmul_rn(__fmul_rn(gin, s.gscale), s.dscale);
+  float m, v;
+  uint32_t payload = 0u;
+  if (MODE == DFC_MODE_PACKED) {
+    m = unpack_signed(mw);
+    payload = vw & 0x80000000u;
+    v = u2f(dec_mag(vw & 0x7FFFFFFFu));
+  } else if (MODE == DFC_MODE_SIGNFIBER) {
+    m = u2f(mw);
+    payload = vw & 0x80000000u;
+    v = u2f(vw & 0x7FFFFFFFu);
+  } else {
+    m = u2f(mw);
+    v = u2f(vw);
+  }
+  const float m_new = __fmaf_rn(g, s.omb1, __fmul_rn(m, s.b1));
+  const float v_new = __fmaf_rn(__fmul_rn(s.omb2, g), g, __fmul_rn(v, s.b2));
+  float v_upd;
+  if (MODE == DFC_MODE_PLAIN) {
+    v_upd = v_new;
+    vw = f2u(v_new);
+  } else {
+    const uint32_t mag = f2u(v_new) & 0x7FFFFFFFu;
+    v_upd = u2f(mag);
+    vw = payload | (MODE == DFC_MODE_PACKED ? enc_mag(mag) : mag);
+  }
+  const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(v_upd), s.sbc2), s.eps);
+  const float upd = __fdiv_rn(__fmul_rn(s.nstep, m_new), den);
+  p = __fadd_rn(__fmul_rn(p, s.decay), upd);
+  mw = MODE == DFC_MODE_PACKED ? pack_signed(m_new) : f2u(m_new);
+}
+
+template <bool BF16>
+__device__ __forceinline__ float4 load_grad4(const void* g, int64_t i) {
+  if (BF16) {
+    const uint2 b = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(g) + i));
+    return make_float4(u2f(b.x << 16), u2f(b.x & 0xFFFF0000u), u2f(b.y << 16),
+                       u2f(b.y & 0xFFFF0000u));
+  }
+  return __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(g) + i));
+}
+
+template <bool BF16>
+__device__ __forceinline__ float load_grad1(const void* g, int64_t i) {
+  if (BF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(g)[i]);
+  return static_cast<const float*>(g)[i];
+}
+
+template <int MODE>
+__device__ __forceinline__ void step4(const Scalars& s, float4& P, const float4& G, uint4& M,
+                                      uint4& V) {
+  step_elem<MODE>(s, P.x, G.x, M.x, V.x);
+  step_elem<MODE>(s, P.y, G.y, M.y, V.y);
+  step_elem<MODE>(s, P.z, G.z, M.z, V.z);
+  step_elem<MODE>(s, P.w, G.w, M.w, V.w);
+}
+
+template <int MODE, bool BF16>
+__device__ __forceinline__ void tile_full_vec(const SegArg& sg, int64_t base, const Scalars& s) {
+  float4 P[kUnroll], G[kUnroll];
+  uint4 M[kUnroll], V[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
+    P[u] = __ldcs(reinterpret_cast<const float4*>(sg.p + i));
+    G[u] = load_grad4<BF16>(sg.g, i);
+    M[u] = __ldcs(reinterpret_cast<const uint4*>(sg.m + i));
+    V[u] = __ldcs(reinterpret_cast<const uint4*>(sg.v + i));
+  }
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
+    step4<MODE>(s, P[u], G[u], M[u], V[u]);
+    __stcs(reinterpret_cast<float4*>(sg.p + i), P[u]);
+    __stcs(reinterpret_cast<uint4*>(sg.m + i), M[u]);
+    __stcs(reinterpret_cast<uint4*>(sg.v + i), V[u]);
+  }
+}
+
+template <int MODE, bool BF16>
+__device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int64_t count,
+                                             bool vec, const Scalars& s) {
+  int64_t done = 0;
+  if (vec) {
+    const int64_t nv = count / kVec;
+    for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
+      const int64_t i = base + j * kVec;
+      float4 P = __ldcs(reinterpret_cast<const float4*>(sg.p + i));
+      const float4 G = load_grad4<BF16>(sg.g, i);
+      uint4 M = __ldcs(reinterpret_cast<const uint4*>(sg.m + i));
+      uint4 V = __ldcs(reinterpret_cast<const uint4*>(sg.v + i));
+      step4<MODE>(s, P, G, M, V);
+      __stcs(reinterpret_cast<float4*>(sg.p + i), P);
+      __stcs(reinterpret_cast<uint4*>(sg.m + i), M);
+      __stcs(reinterpret_cast<uint4*>(sg.v + i), V);
+    }
+    done = nv * kVec;
+  }
+  for (int64_t j = done + threadIdx.x; j < count; j += kThreads) {
+    const int64_t i = base + j;
+    float p = sg.p[i];
+    uint32_t m = sg.m[i], v = sg.v[i];
+    step_elem<MODE>(s, p, load_grad1<BF16>(sg.g, i), m, v);
+    sg.p[i] = p;
+    sg.m[i] = m;
+    sg.v[i] = v;
+  }
+}
+
+template <int MODE, int MAXS, int MAXH>
+__global__ void __launch_bounds__(kThreads)
+    step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
+  const int32_t t = static_cast<int32_t>(blockIdx.x);
+  int lo = 0, hi = b.n_segs;  // tile_base[lo] <= t < tile_base[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
+  }
+  const SegArg& sg = b.seg[lo];
+  const DfcHyper& h = b.hyper[sg.hyper];
+  Scalars s;
+  s.b1 = h.beta1;
+  s.omb1 = h.one_minus_beta1;
+  s.b2 = h.beta2;
+  s.omb2 = h.one_minus_beta2;
+  s.sbc2 = h.sqrt_bc2;
+  s.eps = h.eps;
+  s.decay = h.decay;
+  s.nstep = h.neg_step_size;
+  s.gscale = h.grad_scale;
+  s.dscale = b.dev_scale ? *b.dev_scale : 1.0f;
+
+  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+  const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
+  const bool vec = (sg.flags & kFlagVec) != 0;
+  if (sg.flags & kFlagBf16) {
+    if (vec && count == kTile) tile_full_vec<MODE, true>(sg, base, s);
+    else tile_partial<MODE, true>(sg, base, count, vec, s);
+  } else {
+    if (vec && count == kTile) tile_full_vec<MODE, false>(sg, base, s);
+    else tile_partial<MODE, false>(sg, base, count, vec, s);
+  }
+}
+
+template <int MAXS, int MAXH>
+int launch_batch(StepBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
+  const int32_t tiles = b.tile_base[b.n_segs];
+  if (tiles == 0) return DFC_OK;
+  switch (mode) {
+    case DFC_MODE_PLAIN:
+      step_kernel<DFC_MODE_PLAIN, MAXS, MAXH><<<tiles, kThreads, 0, st>>>(b);
+      break;
+    case DFC_MODE_SIGNFIBER:
+      step_kernel<DFC_MODE_SIGNFIBER, MAXS, MAXH><<<tiles, kThreads, 0, st>>>(b);
+      break;
+    default:
+      step_kernel<DFC_MODE_PACKED, MAXS, MAXH><<<tiles, kThreads, 0, st>>>(b);
+      break;
+  }
+  return launch_status();
+}
+
+int validate(const DfcSegment& s, int32_t n_hypers) {
+  if (s.numel < 0) return DFC_ERR_SIZE;
+  if (s.numel == 0) return DFC_OK;
+  if (!s.param || !s.grad || !s.exp_avg || !s.exp_avg_sq) return DFC_ERR_NULL;
+  if (s.hyper < 0 || s.hyper >= n_hypers) return DFC_ERR_HYPER;
+  if (s.grad_dtype != DFC_GRAD_F32 && s.grad_dtype != DFC_GRAD_BF16) return DFC_ERR_DTYPE;
+  const uintptr_t ga = s.grad_dtype == DFC_GRAD_BF16 ? 2 : 4;
+  if (!aligned(s.param, 4) || !aligned(s.exp_avg, 4) || !aligned(s.exp_avg_sq, 4) ||
+      !aligned(s.grad, ga))
+    return DFC_ERR_ALIGN;
+  if ((s.numel + kTile - 1) / kTile > INT32_MAX / 2) return DFC_ERR_SIZE;
+  return DFC_OK;
+}
+
+SegArg to_arg(const DfcSegment& s, int32_t local_hyper) {
+  SegArg a;
+  a.p = s.param;
+  a.g = s.grad;
+  a.m = s.exp_avg;
+  a.v = s.exp_avg_sq;
+  a.n = s.numel;
+  a.hyper = local_hyper;
+  const bool bf16 = s.grad_dtype == DFC_GRAD_BF16;
+  const bool vec = aligned(s.param, 16) && aligned(s.exp_avg, 16) && aligned(s.exp_avg_sq, 16) &&
+                   aligned(s.grad, bf16 ? 8 : 16);
+  a.flags = (bf16 ? kFlagBf16 : 0) | (vec ? kFlagVec : 0);
+  return a;
+}
+
+// Pack segments into as few launches as the per-launch capacity allows.  A
+// batch closes when it holds MAXS segments, MAXH distinct hyper sets, or
+// would pass INT32_MAX tiles.
+template <int MAXS, int MAXH>
+int run_batches(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32_t n_hypers,
+                int32_t mode, const float* dscale, cudaStream_t st) {
+  StepBatch<MAXS, MAXH> b;
+  std::vector<int32_t> local(static_cast<size_t>(n_hypers), -1);
+  std::vector<int32_t> used;
+  auto reset = [&]() {
+    for (int32_t g : used) local[g] = -1;
+    used.clear();
+    b.dev_scale = dscale;
+    b.n_segs = 0;
+    b.tile_base[0] = 0;
+  };
+  reset();
+  for (int32_t i = 0; i < n; ++i) {
+    const DfcSegment& s = segs[i];
+    if (s.numel == 0) continue;
+    const int32_t tiles = static_cast<int32_t>((s.numel + kTile - 1) / kTile);
+    const bool need_hyper = local[s.hyper] < 0;
+    if (b.n_segs == MAXS || (need_hyper && static_cast<int>(used.size()) == MAXH) ||
+        b.tile_base[b.n_segs] > INT32_MAX - tiles) {
+      int rc = launch_batch(b, mode, st);
+      if (rc != DFC_OK) return rc;
+      reset();
+    }
+    if (local[s.hyper] < 0) {
+      local[s.hyper] = static_cast<int32_t>(used.size());
+      b.hyper[used.size()] = hypers[s.hyper];
+      used.push_back(s.hyper);
+    }
+    b.seg[b.n_segs] = to_arg(s, local[s.hyper]);
+    b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
+    ++b.n_segs;
+  }
+  return b.n_segs ? launch_batch(b, mode, st) : DFC_OK;
+}
+
+// ---- moment-format conversion -------------------------------------------
+template <bool PACK>
+__global__ void convert_kernel(uint32_t* w, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint32_t x = w[i];
+    const uint32_t sign = x & 0x80000000u;
+    w[i] = sign | (PACK ? enc_mag(x & 0x7FFFFFFFu) : dec_mag(x & 0x7FFFFFFFu));
+  }
+}
+
+int convert(uint32_t* w, int64_t n, bool pack, void* stream) {
+  if (n < 0) return DFC_ERR_SIZE;
+  if (n == 0) return DFC_OK;
+  if (!w) return DFC_ERR_NULL;
+  if (!aligned(w, 4)) return DFC_ERR_ALIGN;
+  const int64_t want = (n + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, 148 * 16));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pack) convert_kernel<true><<<blocks, 256, 0, st>>>(w, n);
+  else convert_kernel<false><<<blocks, 256, 0, st>>>(w, n);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace dfc
+
+extern "C" int dfc_mt_step(const DfcSegment* segments, int32_t n_segments, const DfcHyper* hypers,
+                           int32_t n_hypers, int32_t mode, const float* device_grad_scale,
+                           void* stream) {
+  using namespace dfc;
+  if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
+  if (mode != DFC_MODE_PLAIN && mode != DFC_MODE_SIGNFIBER && mode != DFC_MODE_PACKED)
+    return DFC_ERR_MODE;
+  if (n_segments == 0) return DFC_OK;
+  if (!segments || (!hypers && n_hypers > 0)) return DFC_ERR_NULL;
+  for (int32_t i = 0; i < n_segments; ++i) {
+    const int rc = validate(segments[i], n_hypers);
+    if (rc != DFC_OK) return rc;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_segments <= kSmallSegs && n_hypers <= kSmallHypers)
+    return run_batches<kSmallSegs, kSmallHypers>(segments, n_segments, hypers, n_hypers, mode,
+                                                 device_grad_scale, st);
+  return run_batches<kLargeSegs, kLargeHypers>(segments, n_segments, hypers, n_hypers, mode,
+                                               device_grad_scale, st);
+}
+
+// The sign of a first-moment word and the payload bit of a second-moment word
+// both live in bit 31 and pass through unchanged, so the conversion is the
+// same for both; `second` is accepted for symmetry with the Python API.
+extern "C" int dfc_pack_moments(uint32_t* words, int64_t n, int32_t second, void* stream) {
+  (void)second;
+  return dfc::convert(words, n, true, stream);
+}
+
+extern "C" int dfc_unpack_moments(uint32_t* words, int64_t n, int32_t second, void* stream) {
+  (void)second;
+  return dfc::convert(words, n, false, stream);
+}

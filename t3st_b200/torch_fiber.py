@@ -1,0 +1,382 @@
+"""B200 drop-in for the reference's ``torch_fiber`` module (YellowJune/T3st,
+remote/torch_fiber.py): ``DFCAdamW``, ``TorchSignFiberChannel``,
+``local_fiber_capacity`` and the two bit masks, with the same names,
+arguments, state layout and exceptions.
+
+The step itself runs as one fused multi-tensor CUDA launch through the C ABI
+of libdfc_b200.so (``dfc_mt_step``); there is no CPU path and no eager
+fallback: CPU tensors or a missing library raise.
+
+Additive options (defaults reproduce the reference):
+  moment_format="packed"  keep each moment word as bf16-high + 16-bit
+                          error-feedback residual-low (bit 31 of the second
+                          moment still carries the payload bit);
+  max_grad_norm=x         clip by the global gradient norm, computed on the
+                          device (warp-shuffle statistics kernel), applied
+                          inside the step kernel; no host synchronisation.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Iterable
+
+import numpy as np
+import torch
+
+from . import _lib
+
+SIGN_MASK_I32 = -2147483648
+MAGNITUDE_MASK_I32 = 2147483647
+
+_FORMATS = ("fp32", "packed")
+
+
+def _is_dense(t: torch.Tensor) -> bool:
+    """True when t's elements occupy one gap-free block of memory in some
+    dimension order (contiguous, channels_last, any permutation)."""
+    if t.is_contiguous():
+        return True
+    dims = sorted((st, sz) for st, sz in zip(t.stride(), t.shape) if sz != 1)
+    expect = 1
+    for st, sz in dims:
+        if st != expect:
+            return False
+        expect *= sz
+    return True
+
+
+def hyper_row(lr: float, betas, eps: float, weight_decay: float, step: int,
+              grad_scale: float = 1.0) -> tuple:
+    """FP32 scalars of one parameter's update (remote/torch_fiber.py:75-116).
+
+    Every value is formed in double, as the reference does in Python, and is
+    rounded once to f32 when stored -- which is what PyTorch does when a
+    Python float meets an FP32 tensor: ``mul_(beta1)`` (:98),
+    ``add_(alpha=1-beta1)`` (:98), ``mul_(beta2)``/``addcmul_(value=1-beta2)``
+    (:99), ``div_(sqrt(bc2))`` and ``add_(eps)`` (:112), ``mul_(1-lr*wd)``
+    only when wd != 0 (:114-115; multiplying by 1.0 is exact, so the skip is
+    decay=1) and ``addcdiv_(value=-lr/bc1)`` (:116).
+    """
+    beta1, beta2 = float(betas[0]), float(betas[1])
+    bc1 = 1.0 - beta1 ** step
+    bc2 = 1.0 - beta2 ** step
+    decay = (1.0 - lr * weight_decay) if weight_decay else 1.0
+    return (beta1, 1.0 - beta1, beta2, 1.0 - beta2, math.sqrt(bc2), eps, decay,
+            -(lr / bc1), grad_scale, (0.0, 0.0, 0.0))
+
+
+class DFCAdamW(torch.optim.Optimizer):
+    """AdamW with one exact payload bit per FP32 second-moment coordinate.
+
+    Same constructor, ``step``, ``state_dict``/``load_state_dict``,
+    ``initialize_state``, ``second_moment_tensors`` and
+    ``payload_bit_capacity`` as remote/torch_fiber.py:22-117.
+    """
+
+    def __init__(
+        self,
+        params: Iterable[torch.nn.Parameter],
+        lr: float = 1e-3,
+        betas: tuple[float, float] = (0.9, 0.999),
+        eps: float = 1e-8,
+        weight_decay: float = 0.0,
+        enable_fiber: bool = True,
+        *,
+        moment_format: str = "fp32",
+        max_grad_norm: float | None = None,
+    ):
+        if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
+            raise ValueError("invalid AdamW hyperparameters")
+        if moment_format not in _FORMATS:
+            raise ValueError(f"moment_format must be one of {_FORMATS}")
+        if max_grad_norm is not None and not max_grad_norm > 0:
+            raise ValueError("max_grad_norm must be positive")
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self.enable_fiber = bool(enable_fiber)
+        self.moment_format = moment_format
+        self.max_grad_norm = max_grad_norm
+        self._plan_key = None
+        self._plan = None
+        self.initialize_state()
+
+    # ---- state (remote/torch_fiber.py:41-66) ----
+    @torch.no_grad()
+    def initialize_state(self) -> None:
+        for group in self.param_groups:
+            for parameter in group["params"]:
+                if parameter.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+                    raise TypeError("DFCAdamW expects floating parameters")
+                state = self.state[parameter]
+                if not state:
+                    state["step"] = 0
+                    state["exp_avg"] = torch.zeros_like(
+                        parameter, dtype=torch.float32, memory_format=torch.preserve_format)
+                    state["exp_avg_sq"] = torch.zeros_like(
+                        parameter, dtype=torch.float32, memory_format=torch.preserve_format)
+
+    def second_moment_tensors(self) -> list[torch.Tensor]:
+        return [self.state[p]["exp_avg_sq"] for group in self.param_groups for p in group["params"]]
+
+    @property
+    def payload_bit_capacity(self) -> int:
+        return sum(t.numel() for t in self.second_moment_tensors()) if self.enable_fiber else 0
+
+    @property
+    def mode(self) -> int:
+        if self.moment_format == "packed":
+            return _lib.MODE_PACKED
+        return _lib.MODE_SIGNFIBER if self.enable_fiber else _lib.MODE_PLAIN
+
+    def add_param_group(self, param_group) -> None:
+        super().add_param_group(param_group)
+        self._plan_key = None
+        if hasattr(self, "enable_fiber"):
+            self.initialize_state()
+
+    def state_dict(self):
+        sd = super().state_dict()
+        sd["moment_format"] = self.moment_format
+        return sd
+
+    @torch.no_grad()
+    def load_state_dict(self, state_dict) -> None:
+        """Load a checkpoint of this class or of the reference; moment words
+        are converted when the checkpoint's format differs from this
+        optimizer's (reference checkpoints are FP32)."""
+        saved_format = state_dict.get("moment_format", "fp32")
+        if saved_format not in _FORMATS:
+            raise ValueError(f"unknown moment_format {saved_format!r} in checkpoint")
+        super().load_state_dict(state_dict)
+        self._plan_key = None
+        if saved_format != self.moment_format:
+            convert = (_lib.lib().dfc_pack_moments if self.moment_format == "packed"
+                       else _lib.lib().dfc_unpack_moments)
+            for group in self.param_groups:
+                for p in group["params"]:
+                    st = self.state[p]
+                    for key, second in (("exp_avg", 0), ("exp_avg_sq", 1)):
+                        t = st[key]
+                        if not t.is_cuda:
+                            raise RuntimeError("DFCAdamW state must live on a CUDA device")
+                        with torch.cuda.device(t.device):
+                            _lib.check(convert.__name__, convert(
+                                t.data_ptr(), t.numel(), second,
+                                torch.cuda.current_stream(t.device).cuda_stream))
+
+    # ---- the step (remote/torch_fiber.py:68-117) ----
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+
+        work = []  # (param, state, grad tensor used by the kernel, grad dtype code, group index)
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                g = p.grad
+                if g is None:
+                    continue
+                if g.is_sparse:
+                    raise RuntimeError("DFCAdamW does not support sparse gradients")
+                work.append((p, self.state[p], g, gi))
+        if not work:
+            return loss
+
+        key = tuple((id(p), id(g)) for p, _, g, _ in work)
+        if key != self._plan_key:
+            plan = self._build_plan(work)
+            # a converted or re-laid-out gradient is a copy of this step's
+            # values and cannot be reused next step
+            self._plan, self._plan_key = plan, (key if plan[3] else None)
+        segs, devices, keepalive, _, perm = self._plan
+        if perm is not None:
+            work = [work[i] for i in perm]
+
+        # per-tensor step counters (:85-86) and one hyper set per (group, step)
+        hyper_rows, hyper_index = [], {}
+        hidx = segs["hyper"]
+        for i, (p, state, _, gi) in enumerate(work):
+            s = state["step"] + 1
+            k = (gi, s)
+            j = hyper_index.get(k)
+            if j is None:
+                group = self.param_groups[gi]
+                j = hyper_index[k] = len(hyper_rows)
+                hyper_rows.append(hyper_row(group["lr"], group["betas"], group["eps"],
+                                            group["weight_decay"], s))
+            hidx[i] = j
+        hypers = np.array(hyper_rows, dtype=_lib.HYPER_DTYPE)
+
+        lib = _lib.lib()
+        for dev, sl in devices:
+            with torch.cuda.device(dev):
+                stream = torch.cuda.current_stream(dev).cuda_stream
+                scale_ptr = None
+                if self.max_grad_norm is not None:
+                    scale_ptr = self._clip_scale(segs[sl], dev, stream)
+                _lib.check("dfc_mt_step", lib.dfc_mt_step(
+                    _lib.ptr(segs[sl]), sl.stop - sl.start, _lib.ptr(hypers), len(hypers),
+                    self.mode, scale_ptr, stream))
+        for _, state, _, _ in work:
+            state["step"] += 1
+        del keepalive
+        return loss
+
+    def _build_plan(self, work):
+        """Validate every (param, grad, state) triple and lay out the segment
+        descriptors, grouped by device (one launch per device).
+
+        Returns (segments, [(device, slice)], tensors to keep alive,
+        cacheable, permutation of ``work`` into device order or None)."""
+        order = sorted(range(len(work)), key=lambda i: (work[i][0].device.index or 0, i))
+        perm = None if order == list(range(len(work))) else order
+        if perm is not None:
+            work = [work[i] for i in perm]
+        segs = np.zeros(len(work), dtype=_lib.SEGMENT_DTYPE)
+        keep = []
+        devices = []
+        start = 0
+        for i, (p, state, g, _) in enumerate(work):
+            if not p.is_cuda:
+                raise RuntimeError("DFCAdamW (t3st_b200) runs on CUDA tensors only; "
+                                   "move the model to a CUDA device")
+            if p.dtype != torch.float32:
+                raise NotImplementedError("DFCAdamW (t3st_b200) updates FP32 parameters")
+            if g.device != p.device or g.shape != p.shape:
+                raise RuntimeError("gradient must match its parameter's device and shape")
+            m, v = state["exp_avg"], state["exp_avg_sq"]
+            if not _is_dense(p):
+                raise RuntimeError("DFCAdamW (t3st_b200) needs dense parameters")
+            if g.dtype == torch.bfloat16:
+                code = _lib.GRAD_BF16
+            else:
+                code = _lib.GRAD_F32
+                if g.dtype != torch.float32:
+                    g = g.float()  # remote/torch_fiber.py:83
+            if g.stride() != p.stride():
+                g = torch.empty_like(p, dtype=g.dtype).copy_(g)
+            if m.stride() != p.stride() or v.stride() != p.stride():
+                raise RuntimeError("optimizer state layout differs from its parameter")
+            keep.append(g)
+            segs[i] = (p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), 0, code)
+            if i + 1 == len(work) or work[i + 1][0].device != p.device:
+                devices.append((p.device, slice(start, i + 1)))
+                start = i + 1
+        if self.max_grad_norm is not None and len(devices) > 1:
+            raise NotImplementedError("max_grad_norm needs all parameters on one device")
+        cacheable = all(k is w[2] for k, w in zip(keep, work))
+        return segs, devices, keep, cacheable, perm
+
+    def _clip_scale(self, segs, dev, stream) -> int:
+        lib = _lib.lib()
+        refs = np.zeros(len(segs), dtype=_lib.GRADREF_DTYPE)
+        refs["grad"] = segs["grad"]
+        refs["numel"] = segs["numel"]
+        refs["grad_dtype"] = segs["grad_dtype"]
+        nbytes = lib.dfc_grad_stats_scratch_bytes(_lib.ptr(refs), len(refs))
+        scratch = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=dev)
+        stats = torch.empty(len(refs) * _lib.GRADSTATS_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+        coef = torch.empty(2, dtype=torch.float32, device=dev)
+        _lib.check("dfc_grad_stats", lib.dfc_grad_stats(
+            _lib.ptr(refs), len(refs), stats.data_ptr(), scratch.data_ptr(), nbytes, stream))
+        _lib.check("dfc_clip_coef", lib.dfc_clip_coef(
+            stats.data_ptr(), len(refs), float(self.max_grad_norm), coef.data_ptr(),
+            coef.data_ptr() + 4, stream))
+        self._last_clip = coef  # coef[0] = clip coefficient, coef[1] = total norm
+        return coef.data_ptr()
+
+    @property
+    def last_grad_norm(self) -> torch.Tensor | None:
+        """Device tensor holding the global gradient norm of the last clipped step."""
+        c = getattr(self, "_last_clip", None)
+        return None if c is None else c[1]
+
+
+class TorchSignFiberChannel:
+    """Byte-addressable sign fiber over a DFCAdamW state shard
+    (remote/torch_fiber.py:120-185).  Reads and writes run as one device
+    kernel each (``dfc_fiber_read``/``dfc_fiber_write``) with a single
+    host<->device copy of the packed payload."""
+
+    def __init__(self, optimizer: DFCAdamW):
+        if not optimizer.enable_fiber:
+            raise ValueError("optimizer fiber is disabled")
+        self.optimizer = optimizer
+        self.tensors = optimizer.second_moment_tensors()
+        self.ends = np.cumsum([t.numel() for t in self.tensors], dtype=np.int64)
+        devs = {t.device for t in self.tensors}
+        if any(not d.type == "cuda" for d in devs) or len(devs) > 1:
+            raise RuntimeError("TorchSignFiberChannel (t3st_b200) needs the state on one CUDA device")
+        self.device = next(iter(devs)) if devs else None
+        for t in self.tensors:
+            if not t.is_contiguous() and not _is_dense(t):
+                raise RuntimeError("second-moment tensors must be dense")
+        self._ranges = np.zeros(len(self.tensors), dtype=_lib.WORDRANGE_DTYPE)
+        for i, t in enumerate(self.tensors):
+            self._ranges[i] = (t.data_ptr(), t.numel())
+
+    @property
+    def bit_capacity(self) -> int:
+        return int(self.ends[-1]) if self.ends.size else 0
+
+    @property
+    def byte_capacity(self) -> int:
+        return self.bit_capacity // 8
+
+    def _check(self, start: int, count: int) -> None:
+        if start < 0 or count < 0 or start + count > self.bit_capacity:
+            raise IndexError("fiber range out of bounds")
+
+    def _read_packed(self, start: int, count: int) -> np.ndarray:
+        nbytes = (count + 7) // 8
+        if count == 0:
+            return np.empty(0, dtype=np.uint8)
+        with torch.cuda.device(self.device):
+            out = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            _lib.check("dfc_fiber_read", _lib.lib().dfc_fiber_read(
+                _lib.ptr(self._ranges), len(self._ranges), start, count, out.data_ptr(),
+                torch.cuda.current_stream(self.device).cuda_stream))
+            return out.cpu().numpy()
+
+    def _write_packed(self, start: int, count: int, packed: np.ndarray) -> None:
+        if count == 0:
+            return
+        with torch.cuda.device(self.device):
+            src = torch.from_numpy(np.ascontiguousarray(packed, dtype=np.uint8)).to(self.device)
+            _lib.check("dfc_fiber_write", _lib.lib().dfc_fiber_write(
+                _lib.ptr(self._ranges), len(self._ranges), start, count, src.data_ptr(),
+                torch.cuda.current_stream(self.device).cuda_stream))
+
+    @torch.no_grad()
+    def read_bits(self, start: int, count: int) -> np.ndarray:
+        self._check(start, count)
+        packed = self._read_packed(int(start), int(count))
+        return np.unpackbits(packed, bitorder="little")[:count] if count else packed
+
+    @torch.no_grad()
+    def write_bits(self, start: int, payload: np.ndarray) -> None:
+        bits = np.ascontiguousarray(payload, dtype=np.uint8).reshape(-1)
+        if np.any(bits > 1):
+            raise ValueError("payload must be binary")
+        self._check(start, bits.size)
+        self._write_packed(int(start), bits.size, np.packbits(bits, bitorder="little"))
+
+    def read_bytes(self, start: int, count: int) -> bytes:
+        if start < 0 or count < 0 or start + count > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        return self._read_packed(int(start) * 8, int(count) * 8).tobytes()
+
+    def write_bytes(self, start: int, payload: bytes | bytearray | memoryview) -> None:
+        raw = bytes(payload)
+        if start < 0 or start + len(raw) > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        self._write_packed(int(start) * 8, len(raw) * 8, np.frombuffer(raw, dtype=np.uint8))
+
+
+def local_fiber_capacity(optimizer: DFCAdamW) -> dict[str, int]:
+    """Report capacity for a single optimizer/DDP/FSDP shard (remote/torch_fiber.py:188-191)."""
+    bits = optimizer.payload_bit_capacity
+    return {"payload_bits": bits, "payload_bytes": bits // 8, "state_coordinates": bits}

@@ -1,0 +1,124 @@
+"""The C-ABI library loads, exports what the header declares and rejects bad
+arguments before touching the GPU.  CPU only: every call here fails
+validation, so no CUDA call is made."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from t3st_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "dfc_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dfc_\w+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.dfc_abi_version() == 1
+    for code in range(-9, 1):
+        assert _lib.strerror(code) not in ("", "unknown status")
+    assert _lib.strerror(-100) == "unknown status"
+
+
+def test_struct_sizes_match_header():
+    text = open(HEADER).read()
+    for name, dt in (("DfcSegment", _lib.SEGMENT_DTYPE), ("DfcHyper", _lib.HYPER_DTYPE),
+                     ("DfcGradRef", _lib.GRADREF_DTYPE), ("DfcGradStats", _lib.GRADSTATS_DTYPE)):
+        m = re.search(r"(\d+) bytes\.\s*\*/\s*typedef struct " + name, text)
+        assert m and int(m.group(1)) == dt.itemsize, name
+
+
+def _seg(**kw):
+    s = np.zeros(1, dtype=_lib.SEGMENT_DTYPE)
+    s[0] = (0x10000, 0x20000, 0x30000, 0x40000, 16, 0, 0)
+    for k, v in kw.items():
+        s[0][k] = v
+    return s
+
+
+def test_step_rejects_bad_arguments_before_launch():
+    lib = _lib.lib()
+    h = np.zeros(1, dtype=_lib.HYPER_DTYPE)
+    P = _lib.ptr
+    assert lib.dfc_mt_step(None, -1, None, 0, 0, None, None) == _lib.DFC_ERR_SIZE
+    assert lib.dfc_mt_step(None, 0, None, 0, 7, None, None) == _lib.DFC_ERR_MODE
+    assert lib.dfc_mt_step(None, 0, None, 0, 0, None, None) == _lib.DFC_OK
+    assert lib.dfc_mt_step(None, 1, P(h), 1, 0, None, None) == _lib.DFC_ERR_NULL
+    cases = [
+        (_seg(numel=-1), _lib.DFC_ERR_SIZE),
+        (_seg(param=0), _lib.DFC_ERR_NULL),
+        (_seg(grad=0), _lib.DFC_ERR_NULL),
+        (_seg(hyper=1), _lib.DFC_ERR_HYPER),
+        (_seg(hyper=-1), _lib.DFC_ERR_HYPER),
+        (_seg(grad_dtype=2), _lib.DFC_ERR_DTYPE),
+        (_seg(param=0x10002), _lib.DFC_ERR_ALIGN),
+        (_seg(exp_avg_sq=0x40001), _lib.DFC_ERR_ALIGN),
+        (_seg(grad=0x20002), _lib.DFC_ERR_ALIGN),
+        (_seg(grad=0x20001, grad_dtype=1), _lib.DFC_ERR_ALIGN),
+    ]
+    for segs, want in cases:
+        assert lib.dfc_mt_step(P(segs), 1, P(h), 1, 1, None, None) == want
+    # a bad segment after good ones: nothing is launched
+    two = np.concatenate([_seg(), _seg(numel=-5)])
+    assert lib.dfc_mt_step(P(two), 2, P(h), 1, 1, None, None) == _lib.DFC_ERR_SIZE
+
+
+def test_other_entry_points_reject_bad_arguments():
+    lib = _lib.lib()
+    assert lib.dfc_compress_ef(None, None, None, -1, None) == _lib.DFC_ERR_SIZE
+    assert lib.dfc_compress_ef(None, None, None, 0, None) == _lib.DFC_OK
+    assert lib.dfc_compress_ef(None, 0x1000, 0x2000, 4, None) == _lib.DFC_ERR_NULL
+    assert lib.dfc_compress_ef(0x1002, 0x1000, 0x2000, 4, None) == _lib.DFC_ERR_ALIGN
+    assert lib.dfc_compress_ef(0x1000, 0x1001, 0x2000, 4, None) == _lib.DFC_ERR_ALIGN
+    assert lib.dfc_pack_moments(None, -1, 0, None) == _lib.DFC_ERR_SIZE
+    assert lib.dfc_pack_moments(None, 4, 0, None) == _lib.DFC_ERR_NULL
+    assert lib.dfc_unpack_moments(0x1001, 4, 1, None) == _lib.DFC_ERR_ALIGN
+
+    refs = np.zeros(2, dtype=_lib.GRADREF_DTYPE)
+    refs[0] = (0x1000, 10000, 0, 0)
+    refs[1] = (0x2000, 1, 1, 0)
+    need = lib.dfc_grad_stats_scratch_bytes(_lib.ptr(refs), 2)
+    assert need == 3 * _lib.GRADSTATS_DTYPE.itemsize  # 2 tiles + 1 tile of 8192
+    assert lib.dfc_grad_stats(_lib.ptr(refs), 2, 0x5000, 0x6000, need - 1, None) == _lib.DFC_ERR_SCRATCH
+    assert lib.dfc_grad_stats(_lib.ptr(refs), 2, None, 0x6000, need, None) == _lib.DFC_ERR_NULL
+    refs[1]["grad_dtype"] = 5
+    assert lib.dfc_grad_stats(_lib.ptr(refs), 2, 0x5000, 0x6000, need, None) == _lib.DFC_ERR_DTYPE
+    assert lib.dfc_clip_coef(None, -1, 1.0, None, None, None) == _lib.DFC_ERR_SIZE
+
+    ranges = np.zeros(2, dtype=_lib.WORDRANGE_DTYPE)
+    ranges[0] = (0x1000, 10)
+    ranges[1] = (0x2000, 6)
+    assert lib.dfc_fiber_read(_lib.ptr(ranges), 2, 0, 17, 0x9000, None) == _lib.DFC_ERR_RANGE
+    assert lib.dfc_fiber_read(_lib.ptr(ranges), 2, 10, 7, 0x9000, None) == _lib.DFC_ERR_RANGE
+    assert lib.dfc_fiber_read(_lib.ptr(ranges), 2, -1, 1, 0x9000, None) == _lib.DFC_ERR_RANGE
+    assert lib.dfc_fiber_write(_lib.ptr(ranges), 2, 0, 16, None, None) == _lib.DFC_ERR_NULL
+    ranges[1]["words"] = 0x2002
+    assert lib.dfc_fiber_write(_lib.ptr(ranges), 2, 0, 16, 0x9000, None) == _lib.DFC_ERR_ALIGN
+
+
+def test_library_is_self_contained():
+    """The .so needs no PyTorch library: its dynamic dependencies are the C
+    runtime only (the CUDA runtime is linked in statically)."""
+    import subprocess
+
+    out = subprocess.run(["ldd", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    assert "torch" not in out and "libc10" not in out
