@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the fused DFC-AdamW step (param-updates/s and HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N=1 (default) -- multi-tensor step on one GPU: the 62 FP32 tensors of
+ResNet-18 (CIFAR: 3x3 stem, no max-pool, 10 classes; 11,173,962 params),
+params N(0,0.02), grads N(0,1e-3), packed moments (bf16 high half + 16-bit
+error-feedback residual) warmed for 10 steps, one fused launch per step
+through DFCAdamW.step().
+N>1 (under torchrun) -- ZeRO-1 over the same parameter set: bf16 compressed
+gradients with error feedback, NCCL reduce-scatter, fused step on the
+rank's shard, FP32 all-gather of the params (strong scaling: the model is
+fixed, ranks split it).
+
+Prints one JSON line on rank 0.  Timing: W untimed steps, then K steps
+between barrier + synchronize, CUDA events on the launching stream, max over
+ranks.  Inputs (313 MB per step) are larger than the 126 MB L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "param-updates/s and HBM GB/s (% of 8 TB/s) for fused step at 1/2/4/8 B200"
+UNIT = "param-updates/s"
+STEP_BYTES_PER_PARAM = 28  # p r+w 8, g r 4, m r+w 8, v r+w 8
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+BETAS = (0.9, 0.999)
+LR, EPS, WD = 1e-3, 1e-8, 0.01
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work budget of the cpu_baseline sample")
+    ap.add_argument("--no-clocks", action="store_true",
+                    help="skip the nvidia-smi clock sampler (profiling runs)")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# environment helpers
+# ----------------------------------------------------------------------------
+def measured_hbm_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch from a committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons every 200 ms, in the background."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.samples = []
+        self.error = None
+        try:
+            props = torch.cuda.get_device_properties(device)
+            self.gpu_id = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        except AttributeError:
+            self.gpu_id = str(device.index or 0)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError as e:
+            self.error = str(e)
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+        return self.summary()
+
+    def summary(self):
+        if self.error or not self.samples:
+            return {"error": self.error or "no nvidia-smi samples"}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if s[5 + i].lower().startswith("active")})
+        power = [float(s[3]) for s in self.samples if s[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": max(power) if power else None}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if n_gpus != world:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+def resnet18_params(device, seed=0, align=64):
+    """62 ResNet-18 parameters as views of one flat FP32 buffer (offsets
+    aligned to 64 elements), N(0, 0.02)."""
+    from t3st_b200.workloads import resnet18_cifar_shapes
+
+    shapes = resnet18_cifar_shapes()
+    sizes = [math.prod(s) for s in shapes]
+    offs, o = [], 0
+    for n in sizes:
+        offs.append(o)
+        o += (n + align - 1) // align * align
+    gen = torch.Generator(device=device).manual_seed(seed)
+    flat_p = torch.zeros(o, device=device)
+    flat_g = torch.zeros(o, device=device)
+    params = []
+    for s, n, off in zip(shapes, sizes, offs):
+        p = torch.nn.Parameter(flat_p[off:off + n].view(s))
+        p.data.normal_(0.0, 0.02, generator=gen)
+        p.grad = flat_g[off:off + n].view(s)
+        params.append(p)
+    return params, flat_p, flat_g, gen, sum(sizes)
+
+
+def fill_grads(params, gen, std=1e-3):
+    for p in params:
+        p.grad.normal_(0.0, std, generator=gen)
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline (reference algorithm as PyTorch CPU ops; oracle/torch_port.py)
+# ----------------------------------------------------------------------------
+def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None = None):
+    """Time the reference step restated as CPU torch ops on (a prefix of)
+    the workload's tensors; returns (updates/s, description)."""
+    from oracle import torch_port
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(1)
+    tensors = []
+    total = 0
+    for s in shapes:
+        n = math.prod(s)
+        if max_params is not None and tensors and total + n > max_params:
+            break
+        p = torch.randn(n, generator=gen) * 0.02
+        g = torch.randn(n, generator=gen) * 1e-3
+        m = torch.zeros(n, dtype=torch.int32 if packed else torch.float32)
+        v = torch.zeros(n, dtype=torch.int32 if packed else torch.float32)
+        tensors.append((p, g, m, v))
+        total += n
+
+    def one(step):
+        for p, g, m, v in tensors:
+            if packed:
+                torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
+            else:
+                torch_port.step_fp32(p, g, m, v, LR, BETAS, EPS, WD, step, fiber=True)
+
+    one(1)
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        steps += 1
+        one(steps + 1)
+        el = time.perf_counter() - t0
+        if el >= seconds or (steps >= 3 and el * (steps + 1) / steps > 3 * seconds):
+            break
+    rate = total * steps / el
+    desc = (f"{len(tensors)} of {len(shapes)} ResNet-18 tensors ({total} params), {steps} "
+            f"steps, {'packed' if packed else 'fp32 sign-fiber'} moments, "
+            f"{torch.get_num_threads()} threads")
+    return rate, desc, torch.get_num_threads()
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (restated as torch CPU ops)
+    on the host cores, rank 0 only, K+W bounded steps."""
+    if rank != 0:
+        return
+    from oracle import torch_port
+    from t3st_b200.workloads import resnet18_cifar_shapes
+
+    shapes = resnet18_cifar_shapes()
+    torch.set_num_threads(os.cpu_count() or 1)
+    total_params = sum(math.prod(s) for s in shapes)
+    # calibrate on one full step, then bound the sample so the run takes <~2 min
+    rate_full, _, _ = cpu_port_rate(shapes, 0.5, packed=True)
+    budget = 120.0
+    per_step = budget / max(1, args.steps + args.warmup)
+    max_params = max(4096, min(total_params, int(rate_full * per_step)))
+    gen = torch.Generator().manual_seed(1)
+    tensors, total = [], 0
+    for s in shapes:
+        n = math.prod(s)
+        if tensors and total + n > max_params:
+            break
+        tensors.append((torch.randn(n, generator=gen) * 0.02, torch.randn(n, generator=gen) * 1e-3,
+                        torch.zeros(n, dtype=torch.int32), torch.zeros(n, dtype=torch.int32)))
+        total += n
+    step = 0
+    for _ in range(args.warmup):
+        step += 1
+        for p, g, m, v in tensors:
+            torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step += 1
+        for p, g, m, v in tensors:
+            torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
+    el = time.perf_counter() - t0
+    value = total * args.steps / el
+    sample = (f"{len(tensors)} of {len(shapes)} ResNet-18 (CIFAR) tensors, {total} of "
+              f"{total_params} params per step, packed moments, torch CPU ops")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "resnet18-cifar multi-tensor DFC-AdamW step (reference CPU path)",
+                   "tensors": len(shapes), "params": total_params, "moment_format": "packed"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# our arm, one GPU
+# ----------------------------------------------------------------------------
+def run_single(args, device):
+    from t3st_b200 import DFCAdamW
+    from t3st_b200.workloads import resnet18_cifar_shapes
+
+    params, flat_p, flat_g, gen, n_params = resnet18_params(device)
+    opt = DFCAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
+                   moment_format="packed")
+    for _ in range(10):  # warm the packed moments with fresh gradients
+        fill_grads(params, gen)
+        opt.step()
+    fill_grads(params, gen)
+    for _ in range(max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    sampler = None if args.no_clocks else ClockSampler(device).start()
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter()
+    for i in range(K):
+        starts[i].record(stream)
+        opt.step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t_wall
+    clocks = {"skipped": "--no-clocks"}
+    if sampler is not None:
+        # keep the GPU busy with the same step while the clock sampler
+        # collects enough samples (untimed)
+        t_extra = time.perf_counter()
+        while time.perf_counter() - t_extra < max(0.0, 1.5 - wall):
+            for _ in range(200):
+                opt.step()
+            torch.cuda.synchronize()
+        clocks = sampler.stop()
+
+    total_ms = starts[0].elapsed_time(ends[-1])
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    kernel_ms = statistics.median(per_step_ms)
+    value = n_params * K / (total_ms / 1e3)
+    launches_per_step = 1  # 62 segments, 1 hyper set: one dfc_mt_step launch
+
+    peak, peak_kind = measured_hbm_peak()
+    algo_bytes = STEP_BYTES_PER_PARAM * n_params
+    achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
+    traffic = profiled_traffic("dfc_step_resnet18.md")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {
+            "workload": "resnet18-cifar multi-tensor DFC-AdamW step: 62 FP32 tensors, "
+                        "11,173,962 params, packed moments (bf16 hi + 16-bit residual lo), "
+                        "FP32 grads, one fused launch per step via DFCAdamW.step()",
+            "tensors": len(params), "params": n_params, "moment_format": "packed",
+            "algorithmic_bytes_per_param": STEP_BYTES_PER_PARAM,
+            "l2": "inputs 313 MB per step > 126 MB L2 (no flush)",
+            "parallelism": "single GPU",
+        },
+        "hbm_gbs": algo_bytes * K / (total_ms / 1e3) / 1e9,
+        "hbm_pct_of_8tbs": 100.0 * algo_bytes * K / (total_ms / 1e3) / 1e9 / NOMINAL_HBM_GBS,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": traffic,
+                     "kernel": "dfc::step_kernel<PACKED> (median per-step event interval)"},
+        "gpu_launches": K * launches_per_step,
+        "clocks": clocks,
+        "host_wall_ms_per_step": wall / K * 1e3,
+    }
+
+    if not args.no_e2e:
+        line["e2e"] = run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K)
+    if not args.no_cpu_baseline:
+        rate, desc, cores = cpu_port_rate(resnet18_cifar_shapes(), args.cpu_seconds, packed=True)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": desc}
+    return line
+
+
+def run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K):
+    """Same step through the public API with the gradients coming from and
+    the updated params going to pinned host memory every step."""
+    host_g = torch.empty(flat_g.numel(), dtype=torch.float32, pin_memory=True)
+    host_p = torch.empty(flat_p.numel(), dtype=torch.float32, pin_memory=True)
+    host_g.copy_(flat_g.cpu())
+    stream = torch.cuda.current_stream(device)
+    Ke = max(3, min(K, 300))
+    for _ in range(3):
+        flat_g.copy_(host_g, non_blocking=True)
+        opt.step()
+        host_p.copy_(flat_p, non_blocking=True)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(Ke):
+        flat_g.copy_(host_g, non_blocking=True)
+        opt.step()
+        host_p.copy_(flat_p, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"value": n_params * Ke / (ms / 1e3), "unit": UNIT, "steps": Ke,
+            "h2d_bytes_per_step": flat_g.numel() * 4, "d2h_bytes_per_step": flat_p.numel() * 4,
+            "path": "DFCAdamW.step() with grads H2D from pinned host and params D2H to pinned host"}
+
+
+def main():
+    args = parse_args()
+    rank, world, local = (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+                          int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world == 1:
+        line = run_single(args, device)
+    else:
+        from t3st_b200.zero_bench import run_sharded
+
+        line = run_sharded(args, rank, world, device)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -61,9 +61,10 @@ extern "C" {
 #define DFC_MODE_SIGNFIBER 1
 /* Packed words: high 16 bits = moment rounded to the nearest bf16 (ties away
  * from zero), low 16 bits = signed residual in FP32 ulps, so that
- * fp32 = (hi << 16) + (int16)lo exactly.  Bit 31 of the first moment is its
- * sign; bit 31 of the second moment is the payload bit. No counterpart in
- * the reference (it stores FP32 moments). */
+ * fp32 = (hi << 16) + (int16)lo exactly; a NaN is stored as the canonical
+ * word 0x7FC00000.  Bit 31 of the first moment is its sign; bit 31 of the
+ * second moment is the payload bit.  No counterpart in the reference (it
+ * stores FP32 moments). */
 #define DFC_MODE_PACKED 2
 
 /* ---- gradient element types ---- */

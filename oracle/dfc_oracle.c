@@ -25,15 +25,15 @@
  * Packed moment word (bf16 high half + 16-bit error-feedback residual low
  * half).  For an FP32 magnitude a (31 bits):
  *     enc(a) = a + ((a & 0x8000) << 1)        for a <= 0x7F800000
- *     enc(a) = a | 0x00400000                 for NaN
+ *     enc(a) = 0x7FC00000                     for NaN (canonical quiet NaN)
  * so the high half is a rounded to the nearest bf16 (ties away from zero) and
  * the low half, read as a signed int16, is the residual in units of the FP32
  * ulp: dec(W) = (hi << 16) + (int16)lo, clamped to [0, 0x7F800000] (NaN words,
  * hi > 0x7F80, decode to themselves).  Every 16-bit residual pattern is a
- * valid residual, and dec(enc(a)) == a for every FP32 value except that NaNs
- * come back quiet.  The first moment keeps its sign in bit 31; the second
- * moment keeps the reference's payload bit in bit 31 and its magnitude in the
- * rest.
+ * valid residual, and dec(enc(a)) == a for every non-NaN FP32 value.  The
+ * first moment keeps its sign in bit 31 (a NaN is stored as +NaN, so CPU and
+ * GPU NaN patterns agree); the second moment keeps the reference's payload
+ * bit in bit 31 and its magnitude in the rest.
  *
  * Compressed gradient with error feedback.  s = g + e, c = high half of
  * enc(s) (bf16, contiguous for the collective), q = low half (the residual
@@ -73,8 +73,15 @@ static inline float u2f(uint32_t u) {
 
 /* ---- packed word: magnitude encode/decode (31-bit values) ---- */
 uint32_t orc_enc_mag(uint32_t a) {
-  if (a > 0x7F800000u) return a | 0x00400000u;
+  if (a > 0x7F800000u) return 0x7FC00000u;
   return a + ((a & 0x8000u) << 1);
+}
+
+/* signed value -> packed word; NaN becomes the canonical +NaN word */
+static inline uint32_t enc_signed_bits(uint32_t b) {
+  uint32_t a = b & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return 0x7FC00000u;
+  return (b & 0x80000000u) | orc_enc_mag(a);
 }
 
 uint32_t orc_dec_mag(uint32_t w) {
@@ -86,10 +93,7 @@ uint32_t orc_dec_mag(uint32_t w) {
   return (uint32_t)r;
 }
 
-uint32_t orc_pack_signed(float x) {
-  uint32_t b = f2u(x);
-  return (b & 0x80000000u) | orc_enc_mag(b & 0x7FFFFFFFu);
-}
+uint32_t orc_pack_signed(float x) { return enc_signed_bits(f2u(x)); }
 
 float orc_unpack_signed(uint32_t w) {
   return u2f((w & 0x80000000u) | orc_dec_mag(w & 0x7FFFFFFFu));
@@ -182,8 +186,7 @@ static inline float ef_residual(uint16_t c, uint16_t q) {
 void orc_compress_ef(const float* g, uint16_t* c, uint16_t* q, int64_t n) {
   for (int64_t i = 0; i < n; ++i) {
     float s = g[i] + ef_residual(c[i], q[i]);
-    uint32_t b = f2u(s);
-    uint32_t w = (b & 0x80000000u) | orc_enc_mag(b & 0x7FFFFFFFu);
+    uint32_t w = enc_signed_bits(f2u(s));
     c[i] = (uint16_t)(w >> 16);
     q[i] = (uint16_t)(w & 0xFFFFu);
   }

@@ -33,11 +33,18 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as
 //   enc(a) = a + ((a & 0x8000) << 1)   (a <= +Inf: the high half becomes a
 //            rounded to the nearest bf16, ties away from zero, and the low
 //            half -- unchanged -- read as int16 is the residual in ulps)
-//   enc(a) = a | 0x00400000            (NaN: quieted, residual kept)
+//   enc(a) = 0x7FC00000                (NaN: the canonical quiet NaN, so the
+//            CPU and GPU words agree whatever NaN the arithmetic produced)
 // dec(w) = (hi << 16) + (int16)lo, clamped to [0, +Inf]; hi > 0x7F80 is a NaN
 // and decodes to itself.  dec(enc(a)) == a for every non-NaN a.
 __device__ __forceinline__ uint32_t enc_mag(uint32_t a) {
-  return a > 0x7F800000u ? (a | 0x00400000u) : a + ((a & 0x8000u) << 1);
+  return a > 0x7F800000u ? 0x7FC00000u : a + ((a & 0x8000u) << 1);
+}
+
+// Signed value bits -> packed word; a NaN becomes the canonical +NaN word.
+__device__ __forceinline__ uint32_t enc_signed_bits(uint32_t b) {
+  const uint32_t a = b & 0x7FFFFFFFu;
+  return a > 0x7F800000u ? 0x7FC00000u : (b & 0x80000000u) | (a + ((a & 0x8000u) << 1));
 }
 
 __device__ __forceinline__ uint32_t dec_mag(uint32_t w) {
@@ -46,10 +53,7 @@ __device__ __forceinline__ uint32_t dec_mag(uint32_t w) {
   return (w >> 16) > 0x7F80u ? w : static_cast<uint32_t>(r);
 }
 
-__device__ __forceinline__ uint32_t pack_signed(float x) {
-  uint32_t b = f2u(x);
-  return (b & 0x80000000u) | enc_mag(b & 0x7FFFFFFFu);
-}
+__device__ __forceinline__ uint32_t pack_signed(float x) { return enc_signed_bits(f2u(x)); }
 
 __device__ __forceinline__ float unpack_signed(uint32_t w) {
   return u2f((w & 0x80000000u) | dec_mag(w & 0x7FFFFFFFu));

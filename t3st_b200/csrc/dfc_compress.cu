@@ -18,8 +18,7 @@ constexpr int kThreads = 256;
 
 __device__ __forceinline__ void compress1(float g, uint32_t& c, uint32_t& q) {
   const float s = __fadd_rn(g, ef_residual(c, q));
-  const uint32_t b = f2u(s);
-  const uint32_t w = (b & 0x80000000u) | enc_mag(b & 0x7FFFFFFFu);
+  const uint32_t w = enc_signed_bits(f2u(s));
   c = w >> 16;
   q = w & 0xFFFFu;
 }

@@ -29,10 +29,20 @@
 namespace dfc {
 namespace {
 
-constexpr int kThreads = 256;
+// Tile shape (compile-time; the defaults are the measured best on B200).
+#ifndef DFC_STEP_THREADS
+#define DFC_STEP_THREADS 256
+#endif
+#ifndef DFC_STEP_UNROLL
+#define DFC_STEP_UNROLL 4
+#endif
+#ifndef DFC_STEP_MIN_BLOCKS
+#define DFC_STEP_MIN_BLOCKS 1
+#endif
+constexpr int kThreads = DFC_STEP_THREADS;
 constexpr int kVec = 4;
-constexpr int kUnroll = 4;
-constexpr int kTile = kThreads * kVec * kUnroll;  // 4096 elements per CTA
+constexpr int kUnroll = DFC_STEP_UNROLL;
+constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA
 
 constexpr int32_t kFlagBf16 = 1;
 constexpr int32_t kFlagVec = 2;
@@ -178,7 +188,7 @@ __device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int
 }
 
 template <int MODE, int MAXS, int MAXH>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, DFC_STEP_MIN_BLOCKS)
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
   const int32_t t = static_cast<int32_t>(blockIdx.x);
   int lo = 0, hi = b.n_segs;  // tile_base[lo] <= t < tile_base[hi]

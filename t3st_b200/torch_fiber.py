@@ -157,9 +157,11 @@ class DFCAdamW(torch.optim.Optimizer):
                 for p in group["params"]:
                     st = self.state[p]
                     for key, second in (("exp_avg", 0), ("exp_avg_sq", 1)):
-                        t = st[key]
-                        if not t.is_cuda:
+                        if not st[key].is_cuda:
                             raise RuntimeError("DFCAdamW state must live on a CUDA device")
+                        # load_state_dict may alias the checkpoint's tensors
+                        # (same dtype and device): convert a private copy
+                        t = st[key] = st[key].clone(memory_format=torch.preserve_format)
                         with torch.cuda.device(t.device):
                             _lib.check(convert.__name__, convert(
                                 t.data_ptr(), t.numel(), second,
@@ -345,7 +347,7 @@ class TorchSignFiberChannel:
         if count == 0:
             return
         with torch.cuda.device(self.device):
-            src = torch.from_numpy(np.ascontiguousarray(packed, dtype=np.uint8)).to(self.device)
+            src = torch.from_numpy(np.array(packed, dtype=np.uint8, copy=True)).to(self.device)
             _lib.check("dfc_fiber_write", _lib.lib().dfc_fiber_write(
                 _lib.ptr(self._ranges), len(self._ranges), start, count, src.data_ptr(),
                 torch.cuda.current_stream(self.device).cuda_stream))

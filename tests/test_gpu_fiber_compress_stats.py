@@ -1,0 +1,118 @@
+"""Device sign-fiber I/O, bf16 compression with error feedback and the
+gradient statistics kernels, against the oracle / host bit arithmetic."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from t3st_b200 import DFCAdamW, TorchSignFiberChannel, _lib, kernels
+
+pytestmark = pytest.mark.gpu
+
+
+def _fiber_bits(tensors):
+    return np.concatenate([(t.reshape(-1).view(torch.int32).cpu().numpy().view(np.uint32) >> 31)
+                           .astype(np.uint8) for t in tensors])
+
+
+def test_fiber_bits_and_bytes_over_many_ranges(cuda):
+    rng = np.random.default_rng(7)
+    sizes = [int(s) for s in rng.integers(1, 300, 1500)] + [1, 7, 9, 4099]
+    params = [torch.nn.Parameter(torch.zeros(s, device=cuda)) for s in sizes]
+    opt = DFCAdamW(params)
+    ch = TorchSignFiberChannel(opt)
+    total = ch.bit_capacity
+    bits = rng.integers(0, 2, total, dtype=np.uint8)
+    ch.write_bits(0, bits)
+    np.testing.assert_array_equal(_fiber_bits(opt.second_moment_tensors()), bits)
+    for start, count in [(0, total), (3, 1), (5, 1000), (total - 13, 13), (8 * 77 + 3, 4001)]:
+        np.testing.assert_array_equal(ch.read_bits(start, count), bits[start:start + count])
+    # byte form, unaligned start bit inside tensors
+    payload = rng.bytes(ch.byte_capacity - 5)
+    ch.write_bytes(5, payload)
+    assert ch.read_bytes(5, len(payload)) == payload
+    got = _fiber_bits(opt.second_moment_tensors())[40:40 + 8 * len(payload)]
+    np.testing.assert_array_equal(np.packbits(got, bitorder="little").tobytes(), payload)
+    # partial write leaves neighbours alone
+    before = _fiber_bits(opt.second_moment_tensors())
+    ch.write_bits(1001, np.array([1, 0, 1], np.uint8))
+    after = _fiber_bits(opt.second_moment_tensors())
+    before[1001:1004] = [1, 0, 1]
+    np.testing.assert_array_equal(after, before)
+    # magnitudes untouched by payload writes
+    for t in opt.second_moment_tensors():
+        assert torch.count_nonzero(t.view(torch.int32) & 0x7FFFFFFF) == 0
+
+
+@pytest.mark.parametrize("n,offset", [(1, 0), (4, 0), (4099, 0), (1 << 20, 0), (1000003, 1),
+                                      (77777, 3)])
+def test_compress_matches_oracle_over_steps(cuda, n, offset):
+    rng = np.random.default_rng(n)
+    gbuf = torch.zeros(n + offset, device=cuda)
+    cbuf = torch.zeros(n + offset, dtype=torch.int16, device=cuda)
+    qbuf = torch.zeros(n + offset, dtype=torch.int16, device=cuda)
+    g, c, q = gbuf[offset:], cbuf[offset:], qbuf[offset:]
+    hc = np.zeros(n, np.uint16)
+    hq = np.zeros(n, np.uint16)
+    for step in range(4):
+        x = (rng.standard_t(3, n) * 1e-3).astype(np.float32)
+        if step == 2 and n > 8:
+            x[:3] = [np.inf, np.nan, 1e-40]
+        g.copy_(torch.from_numpy(x))
+        kernels.compress_ef(g, c, q)
+        O.compress_ef(x, hc, hq)
+        np.testing.assert_array_equal(c.cpu().numpy().view(np.uint16), hc)
+        np.testing.assert_array_equal(q.cpu().numpy().view(np.uint16), hq)
+
+
+def test_grad_stats_match_oracle(cuda):
+    rng = np.random.default_rng(8)
+    sizes = [0, 1, 5, 8192, 8193, 100003, 1 << 20]
+    grads = []
+    for i, n in enumerate(sizes):
+        x = (rng.standard_normal(n) * 1e-2).astype(np.float32)
+        if i == 4:
+            x[[3, 77]] = [np.inf, np.nan]
+        grads.append(x)
+    tg = [torch.from_numpy(x).to(cuda) for x in grads]
+    tg.append(torch.from_numpy(grads[5]).to(cuda).bfloat16())
+    stats = kernels.stats_to_numpy(kernels.grad_stats(tg))
+    for i, x in enumerate(grads + [None]):
+        if x is None:
+            x = tg[-1].float().cpu().numpy()
+        s, a, bad = O.grad_stats(x)
+        assert stats[i]["nonfinite"] == bad
+        assert stats[i]["amax"] == np.float32(a)
+        if np.isnan(s):
+            assert np.isnan(stats[i]["sumsq"])
+        else:
+            assert stats[i]["sumsq"] == pytest.approx(s, rel=1e-12, abs=0)
+    # deterministic: the same input gives the same bits
+    again = kernels.stats_to_numpy(kernels.grad_stats(tg))
+    assert again.tobytes() == stats.tobytes()
+
+
+def test_clip_coef_and_clipped_step(cuda):
+    torch.manual_seed(0)
+    shapes = [(300, 77), (1000,), (5,)]
+    params = [torch.nn.Parameter(torch.randn(s, device=cuda) * 0.02) for s in shapes]
+    grads = [torch.randn(s, device=cuda) for s in shapes]
+    p0 = [p.detach().cpu().numpy().copy() for p in params]
+    opt = DFCAdamW(params, lr=1e-3, weight_decay=0.01, max_grad_norm=1.0)
+    for p, g in zip(params, grads):
+        p.grad = g
+    opt.step()
+    torch.cuda.synchronize()
+    coef, norm = opt._last_clip.cpu().numpy()
+    total = np.sqrt(sum(float(np.sum(g.double().cpu().numpy() ** 2)) for g in grads))
+    assert norm == pytest.approx(total, rel=1e-6)
+    assert coef == np.float32(np.float32(1.0) / (np.float32(norm) + np.float32(1e-6)))
+    h = O.reference_hyper(1e-3, (0.9, 0.999), 1e-8, 0.01, 1, grad_scale=float(coef))
+    for p, p_init, g in zip(params, p0, grads):
+        p_ref = p_init.reshape(-1).copy()
+        m = np.zeros(p_ref.size, np.uint32)
+        v = np.zeros(p_ref.size, np.uint32)
+        O.step(O.MODE_SIGNFIBER, h, p_ref, g.cpu().numpy().reshape(-1).copy(), m, v)
+        np.testing.assert_array_equal(p.detach().cpu().numpy().reshape(-1).view(np.uint32),
+                                      p_ref.view(np.uint32))

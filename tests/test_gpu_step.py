@@ -1,0 +1,171 @@
+"""dfc_mt_step through the C ABI against the oracle, bit for bit, on seeded
+random inputs: every moment format, FP32 and bf16 gradients, ragged and
+misaligned segments, several hyper sets, the multi-launch batching, special
+values, and the device-side gradient scale."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from t3st_b200 import _lib, kernels
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [0, 1, 2, 3, 4, 5, 7, 8, 31, 4095, 4096, 4097, 8191, 12291, 65537, 300001]
+
+
+def _rows(k):
+    out = []
+    for j in range(k):
+        lr = [1e-3, 3e-4, 2e-2][j % 3]
+        betas = [(0.9, 0.999), (0.8, 0.95), (0.5, 0.9999)][j % 3]
+        wd = [0.01, 0.0, 0.1][j % 3]
+        eps = [1e-8, 1e-6, 1e-12][j % 3]
+        step = 1 + 7 * j
+        h = O.reference_hyper(lr, betas, eps, wd, step)
+        out.append(h)
+    return out
+
+
+def _row_tuple(h):
+    return (h.beta1, h.one_minus_beta1, h.beta2, h.one_minus_beta2, h.sqrt_bc2, h.eps, h.decay,
+            h.neg_step_size, h.grad_scale)
+
+
+def _make_inputs(rng, n, mode, bf16, specials=False):
+    p = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    g = (rng.standard_t(3, n) * 1e-3).astype(np.float32)
+    g[rng.random(n) < 0.05] = 0.0
+    den = rng.random(n) < 0.01
+    g[den] = (rng.integers(1, 1 << 23, n, dtype=np.uint32) | (rng.integers(0, 2, n, dtype=np.uint32) << 31)).view(np.float32)[den]
+    if specials and n >= 8:
+        g[:4] = [np.inf, -np.inf, np.nan, 3.0e38]
+        p[4] = np.nan
+    m = (rng.standard_normal(n) * 1e-4).astype(np.float32).view(np.uint32)
+    v = (np.abs(rng.standard_normal(n)) * 1e-7).astype(np.float32).view(np.uint32)
+    if mode != O.MODE_PLAIN:
+        v = v | (rng.integers(0, 2, n, dtype=np.uint32) << 31)
+    if mode == O.MODE_PACKED:
+        m = (m & np.uint32(0xFFFF0000)) | rng.integers(0, 1 << 16, n, dtype=np.uint32)
+        v = (v & np.uint32(0xFFFF0000)) | rng.integers(0, 1 << 16, n, dtype=np.uint32)
+    if bf16:
+        gb = (g.view(np.uint32) >> 16).astype(np.uint16)
+        return p, gb, m, v
+    return p, g, m, v
+
+
+def _same(a, b):
+    """Bit equality, with every NaN equal to every NaN (the GPU's NaN
+    pattern is canonical, the CPU propagates the input's)."""
+    a = np.asarray(a).view(np.uint32)
+    b = np.asarray(b).view(np.uint32)
+    fa = a.view(np.float32)
+    fb = b.view(np.float32)
+    both_nan = np.isnan(fa) & np.isnan(fb)
+    return np.all((a == b) | both_nan)
+
+
+def _run_case(dev, sizes, mode, bf16, n_hypers, offset_elems, seed, specials=False, scale=None):
+    rng = np.random.default_rng(seed)
+    hs = _rows(n_hypers)
+    host, dev_tensors = [], []
+    for k, n in enumerate(sizes):
+        p, g, m, v = _make_inputs(rng, n, mode, bf16, specials)
+        off = offset_elems[k % len(offset_elems)]
+        def put(a, dt):
+            buf = torch.zeros(n + off + 4, dtype=dt, device=dev)
+            t = buf[off:off + n]
+            t.copy_(torch.from_numpy(a.view({torch.float32: np.float32, torch.int32: np.int32, torch.int16: np.int16}[dt])))
+            return t
+        tp = put(p, torch.float32)
+        tg = put(g.view(np.int16), torch.int16) if bf16 else put(g, torch.float32)
+        if bf16:
+            tg = tg.view(torch.bfloat16)
+        tm = put(m.view(np.int32), torch.int32)
+        tv = put(v.view(np.int32), torch.int32)
+        host.append((p, g, m, v, k % n_hypers))
+        dev_tensors.append((tp, tg, tm, tv))
+    segs = np.zeros(len(sizes), dtype=_lib.SEGMENT_DTYPE)
+    for k, (tp, tg, tm, tv) in enumerate(dev_tensors):
+        segs[k] = (tp.data_ptr(), tg.data_ptr(), tm.data_ptr(), tv.data_ptr(), sizes[k],
+                   k % n_hypers, _lib.GRAD_BF16 if bf16 else _lib.GRAD_F32)
+    hyp = kernels.hypers([_row_tuple(h) for h in hs])
+    dscale = None
+    if scale is not None:
+        dscale = torch.tensor([scale], dtype=torch.float32, device=dev)
+    kernels.mt_step_raw(segs, hyp, mode, dev, dscale)
+    torch.cuda.synchronize()
+    for k, (p, g, m, v, hi) in enumerate(host):
+        h = hs[hi]
+        if scale is not None:
+            # the kernel applies (g * grad_scale) * scale; grad_scale is 1 here
+            h = O.Hyper(**{**h.__dict__, "grad_scale": float(np.float32(scale))})
+        O.step(mode, h, p, g, m, v)
+        tp, tg, tm, tv = dev_tensors[k]
+        assert _same(tp.cpu().numpy(), p), (k, sizes[k])
+        assert _same(tm.cpu().numpy().view(np.uint32), m), (k, sizes[k])
+        assert _same(tv.cpu().numpy().view(np.uint32), v), (k, sizes[k])
+        if mode != O.MODE_PLAIN:
+            np.testing.assert_array_equal(tv.cpu().numpy().view(np.uint32) >> 31, v >> 31)
+
+
+@pytest.mark.parametrize("mode", [O.MODE_PLAIN, O.MODE_SIGNFIBER, O.MODE_PACKED])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_ragged_aligned(cuda, mode, bf16):
+    _run_case(cuda, SIZES, mode, bf16, n_hypers=3, offset_elems=[0], seed=10 + mode)
+
+
+@pytest.mark.parametrize("mode", [O.MODE_SIGNFIBER, O.MODE_PACKED])
+def test_misaligned_segments_take_the_scalar_path(cuda, mode):
+    _run_case(cuda, SIZES, mode, False, n_hypers=2, offset_elems=[1, 2, 3, 0], seed=20 + mode)
+
+
+def test_bf16_misaligned(cuda):
+    _run_case(cuda, SIZES, O.MODE_PACKED, True, n_hypers=2, offset_elems=[1, 3], seed=31)
+
+
+@pytest.mark.parametrize("mode", [O.MODE_PLAIN, O.MODE_SIGNFIBER, O.MODE_PACKED])
+def test_special_values(cuda, mode):
+    _run_case(cuda, [4096, 4103, 9], mode, False, n_hypers=1, offset_elems=[0], seed=40 + mode,
+              specials=True)
+
+
+def test_many_segments_and_hyper_sets_split_into_launches(cuda):
+    rng = np.random.default_rng(5)
+    sizes = [int(s) for s in rng.integers(1, 700, 1300)]
+    _run_case(cuda, sizes, O.MODE_PACKED, False, n_hypers=40, offset_elems=[0, 1], seed=50)
+
+
+def test_device_grad_scale(cuda):
+    _run_case(cuda, [5000, 77], O.MODE_SIGNFIBER, False, n_hypers=1, offset_elems=[0], seed=60,
+              scale=0.37)
+
+
+def test_pack_unpack_kernels_match_oracle(cuda):
+    rng = np.random.default_rng(6)
+    n = 100003
+    x = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    t = torch.from_numpy(x.view(np.int32)).to(cuda)
+    kernels.pack_moments(t, second=False)
+    want = O.pack_first(x.view(np.float32))
+    np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32), want)
+    kernels.unpack_moments(t, second=True)
+    np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32), O.unpack_second(want))
+
+
+def test_errors_surface_as_exceptions(cuda):
+    p = torch.zeros(17, device=cuda)
+    g = torch.zeros(17, device=cuda)
+    m = torch.zeros(17, dtype=torch.int32, device=cuda)
+    v = torch.zeros(17, dtype=torch.int32, device=cuda)
+    segs = kernels.segments([p], [g], [m], [v], [0])
+    segs["param"][0] += 2  # not 4-byte aligned
+    hyp = kernels.hypers([_row_tuple(O.reference_hyper(1e-3, (0.9, 0.999), 1e-8, 0.0, 1))])
+    with pytest.raises(_lib.DfcError, match="aligned"):
+        kernels.mt_step_raw(segs, hyp, O.MODE_SIGNFIBER, cuda)
+    segs["param"][0] -= 2
+    segs["hyper"][0] = 3
+    with pytest.raises(_lib.DfcError, match="hyper"):
+        kernels.mt_step_raw(segs, hyp, O.MODE_SIGNFIBER, cuda)
+    assert torch.count_nonzero(p) == 0  # nothing ran

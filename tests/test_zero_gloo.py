@@ -1,0 +1,209 @@
+"""ZeRO-1 host logic on CPU gloo ranks (world 2 and 4): flat layout, shard
+segments, compression + reduce-scatter + step + all-gather wiring, hyper
+sets, consolidated checkpoints, the per-rank sign fiber, and failure
+behaviour.  The CUDA kernels are replaced by an oracle-backed backend (test
+infrastructure; the product has no CPU path)."""
+
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+
+class OracleBackend:
+    """Stand-in for t3st_b200.zero.CudaKernels on CPU tensors."""
+
+    def compress_ef(self, g, c, q):
+        O.compress_ef(g.numpy(), c.numpy().view(np.uint16), q.numpy().view(np.uint16))
+
+    def step(self, segments, rows, index, mode, device):
+        for (p, g, m, v), j in zip(segments, index):
+            h = O.Hyper(*rows[j][:9])
+            gg = g.view(torch.int16).numpy().view(np.uint16) if g.dtype == torch.bfloat16 else g.numpy()
+            O.step(mode, h, p.numpy(), gg, m.numpy().view(np.uint32), v.numpy().view(np.uint32))
+
+    def convert(self, words, pack, second):
+        w = words.numpy().view(np.uint32)
+        if second:
+            w[:] = O.pack_second(w) if pack else O.unpack_second(w)
+        else:
+            w[:] = O.pack_first(w.view(np.float32)) if pack else O.unpack_first(w).view(np.uint32)
+
+
+SHAPES = [(33, 17), (17,), (1000,), (5,), (3, 3, 3)]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _grads(rank, step, sizes):
+    rng = np.random.default_rng(1000 * step + rank)
+    return [(rng.standard_normal(n) * 1e-3).astype(np.float32) for n in sizes]
+
+
+def _worker(rank, world, port, fmt, result_q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from t3st_b200.zero import ShardedDFCAdamW
+
+        torch.manual_seed(0)
+        params = [torch.nn.Parameter(torch.randn(s) * 0.02) for s in SHAPES]
+        p0 = [p.detach().numpy().reshape(-1).copy() for p in params]
+        groups = [{"params": params[:3]}, {"params": params[3:], "lr": 3e-4, "weight_decay": 0.0}]
+        opt = ShardedDFCAdamW(groups, lr=1e-3, weight_decay=0.01, moment_format=fmt,
+                              backend=OracleBackend())
+        sizes = [p.numel() for p in params]
+        # payload in this rank's fiber (the shard's real coordinates)
+        prng = np.random.default_rng(rank)
+        payload = []
+        for w in opt.second_moment_tensors():
+            bits = torch.from_numpy(prng.integers(0, 2, w.numel()).astype(np.int32))
+            wi = w.view(torch.int32)
+            wi.copy_((wi & 0x7FFFFFFF) | (bits << 31))
+            payload.append(bits)
+        assert opt.payload_bit_capacity == sum(b.numel() for b in payload)
+
+        # simulation state (every rank simulates the whole job)
+        sim_p = [x.copy() for x in p0]
+        sim_m = [np.zeros(n, np.uint32) for n in sizes]
+        sim_v = [np.zeros(n, np.uint32) for n in sizes]
+        ef_c = [np.zeros(opt.padded, np.uint16) for _ in range(world)]
+        ef_q = [np.zeros(opt.padded, np.uint16) for _ in range(world)]
+        mode = O.MODE_PACKED if fmt == "packed" else O.MODE_SIGNFIBER
+        for step in range(1, 5):
+            opt.zero_grad()
+            for p, g in zip(params, _grads(rank, step, sizes)):
+                p.grad.copy_(torch.from_numpy(g).view_as(p))
+            opt.step()
+            # gather the reduced gradient the step used, from every shard
+            red = torch.empty(opt.padded, dtype=torch.bfloat16)
+            dist.all_gather_into_tensor(red, opt.shard_grad)
+            red16 = red.view(torch.int16).numpy().view(np.uint16).copy()
+            exact = np.zeros(opt.padded, np.float64)
+            mag = np.zeros(opt.padded, np.float64)
+            for r in range(world):
+                flat = np.zeros(opt.padded, np.float32)
+                for off, g in zip(opt.offsets, _grads(r, step, sizes)):
+                    flat[off:off + g.size] = g
+                O.compress_ef(flat, ef_c[r], ef_q[r])
+                cr = (ef_c[r].astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+                exact += cr
+                mag += np.abs(cr)
+            got = (red16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+            # the collective sums in bf16: each of the world-1 additions rounds
+            assert np.all(np.abs(got - exact) <= mag * 2.0 ** -8 * world + 1e-30)
+            for i, off in enumerate(opt.offsets):
+                gi = 0 if i < 3 else 1
+                lr, wd = (1e-3, 0.01) if gi == 0 else (3e-4, 0.0)
+                h = O.reference_hyper(lr, (0.9, 0.999), 1e-8, wd, step, grad_scale=1.0 / world)
+                O.step(mode, h, sim_p[i], red16[off:off + sizes[i]].copy(), sim_m[i], sim_v[i])
+            for i, p in enumerate(params):
+                np.testing.assert_array_equal(p.detach().numpy().reshape(-1).view(np.uint32),
+                                              sim_p[i].view(np.uint32))
+        # payload kept
+        for w, bits in zip(opt.second_moment_tensors(), payload):
+            assert torch.equal((w.view(torch.int32) >> 31) & 1, bits)
+        # consolidated moments equal the simulation (payload bits aside)
+        full = opt.consolidated_state_dict(to_rank=None)
+        for i in range(len(params)):
+            st = full["state"][i]
+            assert st["step"] == 4
+            np.testing.assert_array_equal(st["exp_avg"].numpy().reshape(-1).view(np.uint32), sim_m[i])
+            got_v = st["exp_avg_sq"].numpy().reshape(-1).view(np.uint32)
+            np.testing.assert_array_equal(got_v & 0x7FFFFFFF, sim_v[i] & 0x7FFFFFFF)
+        # round trip through a fresh optimizer, including a format change
+        params2 = [torch.nn.Parameter(p.detach().clone()) for p in params]
+        other = "fp32" if fmt == "packed" else "packed"
+        opt2 = ShardedDFCAdamW(params2, moment_format=other, backend=OracleBackend())
+        opt2.load_consolidated_state_dict(full)
+        back = opt2.consolidated_state_dict(to_rank=None)
+        opt3 = ShardedDFCAdamW([torch.nn.Parameter(p.detach().clone()) for p in params],
+                               moment_format=fmt, backend=OracleBackend())
+        opt3.load_consolidated_state_dict(back)
+        assert torch.equal(opt3.exp_avg.view(torch.int32), opt.exp_avg.view(torch.int32))
+        assert torch.equal(opt3.exp_avg_sq.view(torch.int32), opt.exp_avg_sq.view(torch.int32))
+        # shard-local checkpoint
+        opt3.load_state_dict(opt.state_dict())
+        # .grad rebinding is refused
+        params[0].grad = torch.zeros_like(params[0])
+        with pytest.raises(RuntimeError, match="owns .grad"):
+            opt.step()
+        dist.barrier()
+        dist.destroy_process_group()
+        result_q.put((rank, "ok"))
+    except BaseException:
+        result_q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,fmt", [(2, "packed"), (2, "fp32"), (4, "packed")])
+def test_zero1_matches_simulation(world, fmt):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fmt, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert results[r] == "ok", results[r]
+
+
+def _dying_worker(rank, world, port, result_q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=3))
+        from t3st_b200.zero import ShardedDFCAdamW
+
+        params = [torch.nn.Parameter(torch.zeros(100))]
+        opt = ShardedDFCAdamW(params, backend=OracleBackend())
+        if rank == 1:
+            result_q.put((rank, "left"))
+            result_q.close()
+            result_q.join_thread()
+            os._exit(0)  # leaves between steps, no collective in flight
+        try:
+            opt.step()
+            result_q.put((rank, "no error"))
+        except RuntimeError as e:
+            result_q.put((rank, "error: " + str(e)[:60]))
+    except BaseException:
+        result_q.put((rank, traceback.format_exc()))
+
+
+def test_lost_rank_surfaces_as_error_not_hang():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("error"), results[0]
