@@ -19,6 +19,7 @@ Additive options (defaults reproduce the reference):
 from __future__ import annotations
 
 import math
+import operator
 from typing import Iterable
 
 import numpy as np
@@ -99,6 +100,7 @@ class DFCAdamW(torch.optim.Optimizer):
         self.max_grad_norm = max_grad_norm
         self._plan_key = None
         self._plan = None
+        self._fast = None
         self.initialize_state()
 
     # ---- state (remote/torch_fiber.py:41-66) ----
@@ -132,6 +134,7 @@ class DFCAdamW(torch.optim.Optimizer):
     def add_param_group(self, param_group) -> None:
         super().add_param_group(param_group)
         self._plan_key = None
+        self._fast = None
         if hasattr(self, "enable_fiber"):
             self.initialize_state()
 
@@ -150,6 +153,7 @@ class DFCAdamW(torch.optim.Optimizer):
             raise ValueError(f"unknown moment_format {saved_format!r} in checkpoint")
         super().load_state_dict(state_dict)
         self._plan_key = None
+        self._fast = None
         if saved_format != self.moment_format:
             convert = (_lib.lib().dfc_pack_moments if self.moment_format == "packed"
                        else _lib.lib().dfc_unpack_moments)
@@ -174,8 +178,15 @@ class DFCAdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        fast = self._fast
+        if fast is not None and fast.try_step(self):
+            return loss
+        self._fast = None
+        self._step_general()
+        return loss
 
-        work = []  # (param, state, grad tensor used by the kernel, grad dtype code, group index)
+    def _step_general(self) -> None:
+        work = []  # (param, state, grad, group index)
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
                 g = p.grad
@@ -185,7 +196,7 @@ class DFCAdamW(torch.optim.Optimizer):
                     raise RuntimeError("DFCAdamW does not support sparse gradients")
                 work.append((p, self.state[p], g, gi))
         if not work:
-            return loss
+            return
 
         key = tuple((id(p), id(g)) for p, _, g, _ in work)
         if key != self._plan_key:
@@ -225,7 +236,9 @@ class DFCAdamW(torch.optim.Optimizer):
         for _, state, _, _ in work:
             state["step"] += 1
         del keepalive
-        return loss
+        n_params = sum(len(g["params"]) for g in self.param_groups)
+        if len(work) == n_params and len(devices) == 1 and self._plan_key is not None:
+            self._fast = _FastPlan(self, work, segs, devices[0][0])
 
     def _build_plan(self, work):
         """Validate every (param, grad, state) triple and lay out the segment
@@ -295,6 +308,78 @@ class DFCAdamW(torch.optim.Optimizer):
         """Device tensor holding the global gradient norm of the last clipped step."""
         c = getattr(self, "_last_clip", None)
         return None if c is None else c[1]
+
+
+_GRAD = operator.attrgetter("grad")
+_DTYPE = operator.attrgetter("dtype")
+_STEP = operator.itemgetter("step")
+_DATA_PTR = torch.Tensor.data_ptr
+_STRIDE = torch.Tensor.stride
+
+
+class _FastPlan:
+    """Steady-state step: every parameter has a gradient, one device, one
+    step count shared by all parameters, the same parameter and gradient
+    storage as the step that built the plan.  Checking that costs a few
+    C-level passes over the parameter list (pointers, dtypes, counters); any
+    mismatch falls back to the general path, which re-validates everything."""
+
+    def __init__(self, opt: "DFCAdamW", work, segs, device):
+        self.params = [w[0] for w in work]
+        self.states = [w[1] for w in work]
+        self.grads = [w[2] for w in work]
+        self.pptrs = list(map(_DATA_PTR, self.params))
+        self.gptrs = list(map(_DATA_PTR, self.grads))
+        self.gdtypes = list(map(_DTYPE, self.grads))
+        self.gstrides = list(map(_STRIDE, self.grads))
+        self.mode = opt.mode
+        self.device = device
+        self.segs = segs.copy()
+        self.segs["hyper"] = [w[3] for w in work]
+        self.hyp = np.zeros(len(opt.param_groups), dtype=_lib.HYPER_DTYPE)
+        self.n_groups = len(opt.param_groups)
+
+    def try_step(self, opt: "DFCAdamW") -> bool:
+        grads = list(map(_GRAD, self.params))
+        try:
+            gptrs = list(map(_DATA_PTR, grads))
+        except TypeError:  # a parameter without gradient
+            return False
+        if gptrs != self.gptrs or list(map(_DATA_PTR, self.params)) != self.pptrs:
+            return False
+        if not all(map(operator.is_, grads, self.grads)):
+            if (list(map(_DTYPE, grads)) != self.gdtypes
+                    or list(map(_STRIDE, grads)) != self.gstrides
+                    or any(map(operator.attrgetter("is_sparse"), grads))):
+                return False
+            self.grads = grads
+        steps = list(map(_STEP, self.states))
+        s = steps[0]
+        if steps.count(s) != len(steps) or opt.mode != self.mode or \
+                len(opt.param_groups) != self.n_groups:
+            return False
+        s += 1
+        for gi, group in enumerate(opt.param_groups):
+            self.hyp[gi] = hyper_row(group["lr"], group["betas"], group["eps"],
+                                     group["weight_decay"], s)
+        dev = self.device
+        lib = _lib.lib()
+        if torch.cuda.current_device() != dev.index:
+            with torch.cuda.device(dev):
+                return self._launch(opt, lib, dev, s)
+        return self._launch(opt, lib, dev, s)
+
+    def _launch(self, opt, lib, dev, s) -> bool:
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        scale_ptr = None
+        if opt.max_grad_norm is not None:
+            scale_ptr = opt._clip_scale(self.segs, dev, stream)
+        _lib.check("dfc_mt_step", lib.dfc_mt_step(
+            _lib.ptr(self.segs), len(self.segs), _lib.ptr(self.hyp), self.n_groups, self.mode,
+            scale_ptr, stream))
+        for st in self.states:
+            st["step"] = s
+        return True
 
 
 class TorchSignFiberChannel:

@@ -169,3 +169,43 @@ def test_errors_surface_as_exceptions(cuda):
     with pytest.raises(_lib.DfcError, match="hyper"):
         kernels.mt_step_raw(segs, hyp, O.MODE_SIGNFIBER, cuda)
     assert torch.count_nonzero(p) == 0  # nothing ran
+
+
+def test_public_step_fast_path_follows_storage_and_grad_changes(cuda):
+    """The steady-state fast path must notice re-pointed parameters, new
+    gradient tensors, missing gradients and diverging step counters."""
+    from t3st_b200 import DFCAdamW
+
+    rng = np.random.default_rng(77)
+    sizes = [1000, 37, 4096]
+    p0 = [(rng.standard_normal(n) * 0.02).astype(np.float32) for n in sizes]
+    params = [torch.nn.Parameter(torch.from_numpy(x.copy()).to(cuda)) for x in p0]
+    opt = DFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed")
+    ref = [dict(p=x.copy(), m=np.zeros(x.size, np.uint32), v=np.zeros(x.size, np.uint32)) for x in p0]
+    steps = [0, 0, 0]
+    group = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    fixed = [torch.zeros(n, device=cuda) for n in sizes]
+    for t in range(12):
+        gs = [(rng.standard_normal(n) * 1e-3).astype(np.float32) for n in sizes]
+        if t < 4:  # same grad tensors every step (fast path by identity)
+            for f, g in zip(fixed, gs):
+                f.copy_(torch.from_numpy(g))
+            for p, f in zip(params, fixed):
+                p.grad = f
+        else:      # new grad tensors every step
+            for p, g in zip(params, gs):
+                p.grad = torch.from_numpy(g).to(cuda)
+        if t == 6:  # re-point a parameter's storage
+            params[0].data = params[0].data.clone()
+        if t == 8:
+            params[1].grad = None
+            gs[1] = None
+        opt.step()
+        O.multi_tensor_step(O.MODE_PACKED, ref, gs, group, steps)
+    torch.cuda.synchronize()
+    for p, r in zip(params, ref):
+        np.testing.assert_array_equal(p.detach().cpu().numpy().view(np.uint32), r["p"].view(np.uint32))
+    for p, r in zip(params, ref):
+        np.testing.assert_array_equal(opt.state[p]["exp_avg"].cpu().numpy().view(np.uint32), r["m"])
+        np.testing.assert_array_equal(opt.state[p]["exp_avg_sq"].cpu().numpy().view(np.uint32), r["v"])
+    assert [opt.state[p]["step"] for p in params] == steps == [12, 11, 12]
