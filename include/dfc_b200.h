@@ -173,6 +173,29 @@ DFC_API int dfc_grad_stats(const DfcGradRef* grads, int32_t n_grads, DfcGradStat
                    size_t scratch_bytes, void* stream);
 
 /*
+ * dfc_grad_stats for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Same records, same kernels and the same
+ * results as dfc_grad_stats, but the per-tile partial records live in a
+ * device array inside the library instead of a caller-provided scratch
+ * buffer, so the call needs nothing but the gradients and `out`.  It exists
+ * for callers that cannot call cudaMalloc or any allocating routine when
+ * they need the statistics (a host runtime whose device memory is all in
+ * its own pool, a plugin whose host forbids device allocations during a
+ * step).
+ * Limit: a call may need at most DFC_GRAD_STATS_STATIC_RECORDS partial
+ * records (one per 8192 elements of each buffer, at least one per buffer);
+ * a larger request returns DFC_ERR_SCRATCH and launches nothing.  The array
+ * (1.5 MiB) is held on every GPU that loads the library until exit.  The
+ * first call on a device, with that device current, looks up the array's
+ * device address; make that first call before any stream capture.  All
+ * calls share the array: calls whose kernels overlap on the GPU race, so
+ * order them on one stream.
+ */
+#define DFC_GRAD_STATS_STATIC_RECORDS 65536
+DFC_API int dfc_grad_stats_noalloc(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* out,
+                                   void* stream);
+
+/*
  * Global-norm clip coefficient from statistics records, on the device:
  * total = sqrt(sum sumsq); coef = min(1, max_norm / (total + 1e-6)).
  * Writes the coefficient to out_coef[0] and the norm to out_norm[0] (either

@@ -29,6 +29,9 @@ DFC_ERR_CUDA = -7
 DFC_ERR_RANGE = -8
 DFC_ERR_SCRATCH = -9
 
+# partial records available to dfc_grad_stats_noalloc (include/dfc_b200.h)
+GRAD_STATS_STATIC_RECORDS = 65536
+
 MODE_PLAIN = 0
 MODE_SIGNFIBER = 1
 MODE_PACKED = 2
@@ -57,7 +60,7 @@ EXPORTS = (
     "dfc_abi_version", "dfc_strerror", "dfc_last_cuda_error", "dfc_mt_step",
     "dfc_pack_moments", "dfc_unpack_moments", "dfc_compress_ef",
     "dfc_grad_stats_scratch_bytes", "dfc_grad_stats", "dfc_clip_coef",
-    "dfc_fiber_read", "dfc_fiber_write",
+    "dfc_fiber_read", "dfc_fiber_write", "dfc_grad_stats_noalloc",
 )
 
 
@@ -90,6 +93,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_clip_coef": ([P, I32, ctypes.c_float, P, P, P], ctypes.c_int),
         "dfc_fiber_read": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_fiber_write": ([P, I32, I64, I64, P, P], ctypes.c_int),
+        "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(h, name)

@@ -1,0 +1,75 @@
+"""dfc_grad_stats_noalloc, the statistics entry point for callers that
+cannot allocate device memory (a host runtime whose device memory all
+belongs to its own pool, a plugin whose host forbids device allocations
+during a step).  It keeps its partial records in a device array inside the
+library, so the caller passes only the gradients and the output records.
+
+The test calls it through the C ABI twice in a row, on different inputs, and
+checks each result against the allocating entry point dfc_grad_stats with the
+tolerance the other statistics tests use (sum of squares to 1e-12 relative,
+max and non-finite count exact).  This file is collected last so that a run
+stopping at the first failure has already run every other test; it also
+passes alone in a fresh process."""
+
+import numpy as np
+import pytest
+import torch
+
+from t3st_b200 import _lib, kernels
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(cuda, seed):
+    rng = np.random.default_rng(seed)
+    sizes = [0, 1, 7, 8192, 8193, 100003, 1 << 20]
+    grads = []
+    for i, n in enumerate(sizes):
+        x = (rng.standard_normal(n) * 10.0 ** rng.uniform(-4, 0)).astype(np.float32)
+        if i == 4 and seed % 2:
+            x[[5, 99]] = [np.inf, np.nan]
+        grads.append(torch.from_numpy(x).to(cuda))
+    grads.append(grads[5].bfloat16())
+    return grads
+
+
+def _noalloc(grads, cuda):
+    refs = kernels.grad_refs(grads)
+    out = torch.full((len(grads) * _lib.GRADSTATS_DTYPE.itemsize,), 0xAB, dtype=torch.uint8,
+                     device=cuda)
+    with torch.cuda.device(cuda):
+        rc = _lib.lib().dfc_grad_stats_noalloc(
+            _lib.ptr(refs), len(refs), out.data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == _lib.DFC_OK, _lib.strerror(rc)
+    return kernels.stats_to_numpy(out)
+
+
+def _check(got, want):
+    np.testing.assert_array_equal(got["nonfinite"], want["nonfinite"])
+    np.testing.assert_array_equal(got["amax"], want["amax"])
+    for a, b in zip(got["sumsq"], want["sumsq"]):
+        if np.isnan(b):
+            assert np.isnan(a)
+        else:
+            assert a == pytest.approx(b, rel=1e-12, abs=0)
+
+
+def test_noalloc_stats_match_the_scratch_entry_point_on_two_calls(cuda):
+    for seed in (1, 2):  # two calls in a row on different inputs
+        grads = _inputs(cuda, seed)
+        want = kernels.stats_to_numpy(kernels.grad_stats(grads))
+        got = _noalloc(grads, cuda)
+        _check(got, want)
+
+
+def test_noalloc_rejects_requests_beyond_the_static_capacity(cuda):
+    g = torch.zeros(16, device=cuda)
+    refs = kernels.grad_refs([g])
+    # claim more elements than the partial-record array can cover; the call
+    # must refuse before launching anything (the pointer is never read)
+    refs["numel"][0] = (_lib.GRAD_STATS_STATIC_RECORDS + 1) * 8192
+    out = torch.empty(_lib.GRADSTATS_DTYPE.itemsize, dtype=torch.uint8, device=cuda)
+    with torch.cuda.device(cuda):
+        rc = _lib.lib().dfc_grad_stats_noalloc(_lib.ptr(refs), 1, out.data_ptr(),
+                                               torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == _lib.DFC_ERR_SCRATCH
