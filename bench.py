@@ -8,14 +8,15 @@ ResNet-18 (CIFAR: 3x3 stem, no max-pool, 10 classes; 11,173,962 params),
 params N(0,0.02), grads N(0,1e-3), packed moments (bf16 high half + 16-bit
 error-feedback residual) warmed for 10 steps, one fused launch per step
 through DFCAdamW.step().
-N>1 (under torchrun) -- ZeRO-1 over the same parameter set: bf16 compressed
-gradients with error feedback, NCCL reduce-scatter, fused step on the
-rank's shard, FP32 all-gather of the params (strong scaling: the model is
-fixed, ranks split it).
+N>1 (under torchrun) -- ZeRO-1 sharded step over a flat 2^30-element FP32
+parameter vector: bf16 compressed gradients with error feedback, NCCL
+reduce-scatter, fused packed step on the rank's 1/N shard, FP32 all-gather
+of the params (strong scaling: the vector is fixed, ranks split its state).
 
 Prints one JSON line on rank 0.  Timing: W untimed steps, then K steps
 between barrier + synchronize, CUDA events on the launching stream, max over
-ranks.  Inputs (313 MB per step) are larger than the 126 MB L2.
+ranks.  Inputs (313 MB per step at N=1, GBs per rank at N>1) are larger
+than the 126 MB L2.
 """
 
 from __future__ import annotations
@@ -454,6 +455,112 @@ def host_overhead_us(opt, n=200) -> float:
     return dt / n * 1e6
 
 
+# ----------------------------------------------------------------------------
+# our arm, N GPUs: ZeRO-1 over a flat 2^30-element parameter vector
+# ----------------------------------------------------------------------------
+ZERO_PARAMS = 1 << 30
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
+
+
+def run_sharded(args, rank, world, device):
+    import torch.distributed as dist
+
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    P = ZERO_PARAMS
+    gen = torch.Generator(device=device).manual_seed(1234)  # same params on every rank
+    param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
+    opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
+                          moment_format="packed")
+    del param
+    ggen = torch.Generator(device=device).manual_seed(100 + rank)  # per-rank gradients
+    opt.flat_grad[:P].normal_(0.0, 1e-3, generator=ggen)
+    for _ in range(max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    K = args.steps
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(device).start() if (rank == 0 and not args.no_clocks) else None
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(K):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    clocks = sampler.stop() if sampler is not None else {"skipped": "rank > 0 or --no-clocks"}
+    value = P * K / (ms / 1e3)
+    # roofline: the slower of this rank's HBM bytes and its NVLink bytes
+    hbm_bytes = 12 * P + 26 * P // world          # compress over P, step over the shard
+    nvl_bytes = 6 * P * (world - 1) // world      # bf16 RS + FP32 AG, per direction
+    peak, peak_kind = measured_hbm_peak()
+    t_hbm = hbm_bytes / (peak * 1e9)
+    t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
+    roof_rate = P / max(t_hbm, t_nvl)
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {
+                "workload": "ZeRO-1 sharded DFC-AdamW step over a flat 2^30-element FP32 "
+                            "parameter vector: bf16 error-feedback compression, NCCL "
+                            "reduce-scatter, fused packed-moment step on the 1/N shard, "
+                            "NCCL FP32 all-gather",
+                "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
+                "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
+            },
+            "roofline": {"bound": "nvlink" if t_nvl > t_hbm else "hbm",
+                         "achieved": value, "peak": roof_rate, "unit": UNIT,
+                         "frac": value / roof_rate,
+                         "hbm_bytes_per_rank": hbm_bytes, "nvlink_bytes_per_rank": nvl_bytes,
+                         "hbm_peak_gbs": peak, "hbm_peak_source": f"{peak_kind} hbm_gbs",
+                         "nvlink_gbs": NVLINK_GBS, "traffic": None},
+            "gpu_launches": K * 2,
+            "clocks": clocks,
+        }
+    if not args.no_e2e:
+        e2e = run_sharded_e2e(opt, P, device, world)
+        if rank == 0:
+            line["e2e"] = e2e
+    return line
+
+
+def run_sharded_e2e(opt, P, device, world, steps=3):
+    """Public API with host buffers: each rank's gradients come from pinned
+    host memory and its updated parameters go back to it every step."""
+    import torch.distributed as dist
+
+    host_g = torch.empty(P, dtype=torch.float32, pin_memory=True)
+    host_p = torch.empty(P, dtype=torch.float32, pin_memory=True)
+    host_g.copy_(opt.flat_grad[:P])
+    stream = torch.cuda.current_stream(device)
+    opt.flat_grad[:P].copy_(host_g, non_blocking=True)
+    opt.step()
+    host_p.copy_(opt.flat_param[:P], non_blocking=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        opt.flat_grad[:P].copy_(host_g, non_blocking=True)
+        opt.step()
+        host_p.copy_(opt.flat_param[:P], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    return {"value": P * steps / (ms / 1e3), "unit": UNIT, "steps": steps,
+            "h2d_bytes_per_step": P * 4, "d2h_bytes_per_step": P * 4,
+            "path": "ShardedDFCAdamW.step() with each rank's grads H2D from pinned host and "
+                    "params D2H to pinned host every step"}
+
+
 def main():
     args = parse_args()
     rank, world, local = (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
@@ -467,8 +574,6 @@ def main():
     if world == 1:
         line = run_single(args, device)
     else:
-        from t3st_b200.zero_bench import run_sharded
-
         line = run_sharded(args, rank, world, device)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)

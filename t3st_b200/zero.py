@@ -1,32 +1,38 @@
 """ZeRO-1 sharded DFC-AdamW across the GPUs of one node.
 
 Every rank holds the full FP32 parameters and computes its own full
-gradient (data parallel); the optimizer state is split into N contiguous
-shards of the flattened parameter vector.  One step:
+gradient (data parallel); the optimizer state is sharded.  The flattened
+parameter vector is cut into buckets of ``bucket_elems`` elements and each
+bucket into N equal pieces; rank r owns piece r of every bucket.  One step,
+per bucket b, pipelined across buckets:
 
-  1. compress the local gradient to bf16 with per-element error feedback
-     (``dfc_compress_ef``; N > 1 only);
-  2. NCCL reduce-scatter (sum) of the bf16 gradients -> this rank's shard;
-  3. fused DFC-AdamW step on the shard (``dfc_mt_step``, bf16 gradients,
-     grad_scale = 1/N to average), packed moment words by default;
-  4. NCCL all-gather of the updated FP32 shard into every rank's parameters.
+  C(b)   compress the local gradient to bf16 with per-element error
+         feedback (``dfc_compress_ef``; when compressing);
+  RS(b)  NCCL reduce-scatter (sum) of the bucket -> this rank's piece;
+  S(b)   fused DFC-AdamW step on the piece (``dfc_mt_step``, bf16 gradients,
+         grad_scale = 1/N to average), packed moment words by default;
+  AG(b)  NCCL all-gather of the updated FP32 piece into every rank's bucket.
+
+The host issues C(0) RS(0), then for each b: C(b+1) RS(b+1), wait RS(b),
+S(b) AG(b).  The collectives run in that order on NCCL's stream and the
+kernels on the caller's stream, so the compression and step of one bucket
+overlap the transfers of its neighbours; the step returns with the caller's
+stream ordered after the last all-gather.
 
 The parameters are re-homed into one flat FP32 buffer (each becomes a view
 of it) and their ``.grad`` into one flat gradient buffer, so the collectives
 run on contiguous memory with no packing copies.  Each parameter starts on a
-16-element boundary and each shard on a 64-element boundary, so every segment
-of the step is 16-byte aligned.  The reference has no distributed code; its
-docstrings only say that FP32 state keeps the payload under DDP/FSDP local
-shards (remote/torch_fiber.py:3-6, 188-191) -- here the sign fiber of a rank
-is the payload bit of its own shard's second-moment words.
+16-element boundary and each piece on a 64-element boundary, so every
+segment of the step is 16-byte aligned.  The reference has no distributed
+code; its docstrings only say that FP32 state keeps the payload under
+DDP/FSDP local shards (remote/torch_fiber.py:3-6, 188-191) -- here the sign
+fiber of a rank is the payload bit of its own pieces' second-moment words.
 """
 
 from __future__ import annotations
 
-import math
 from typing import Iterable
 
-import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -34,29 +40,28 @@ from . import _lib, kernels
 from .torch_fiber import _FORMATS, hyper_row
 
 PARAM_ALIGN = 16   # elements (64 bytes)
-SHARD_ALIGN = 64   # elements (256 bytes)
+PIECE_ALIGN = 64   # elements (256 bytes)
+DEFAULT_BUCKET = 1 << 26  # elements per bucket (256 MB of FP32 parameters)
 
 
 class CudaKernels:
-    """The product backend: libdfc_b200.so kernels on CUDA tensors.  The
-    step's descriptor array is built once (the buffers never move) and only
-    its hyper-set column changes between steps."""
+    """The product backend: libdfc_b200.so kernels on CUDA tensors.  Each
+    bucket's descriptor array is built once (the buffers never move) and
+    only its hyper-set column changes between steps."""
 
     def __init__(self):
-        self._segs = None
-        self._key = None
+        self._segs = {}
 
     def compress_ef(self, grad, comp, resid):
         kernels.compress_ef(grad, comp, resid)
 
-    def step(self, segments, hyper_rows, hyper_index, mode, device):
-        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), p.numel()) for p, g, m, _ in segments)
-        if key != self._key:
-            ps, gs, ms, vs = zip(*segments) if segments else ((), (), (), ())
-            self._segs = kernels.segments(ps, gs, ms, vs, hyper_index)
-            self._key = key
-        self._segs["hyper"] = hyper_index
-        kernels.mt_step_raw(self._segs, kernels.hypers(hyper_rows), mode, device)
+    def step(self, segments, hyper_rows, hyper_index, mode, device, key=0):
+        segs = self._segs.get(key)
+        if segs is None:
+            ps, gs, ms, vs = zip(*segments)
+            segs = self._segs[key] = kernels.segments(ps, gs, ms, vs, hyper_index)
+        segs["hyper"] = hyper_index
+        kernels.mt_step_raw(segs, kernels.hypers(hyper_rows), mode, device)
 
     def convert(self, words, pack: bool, second: bool):
         (kernels.pack_moments if pack else kernels.unpack_moments)(words, second)
@@ -70,6 +75,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     compress_grads  bf16 + error-feedback compression before the
                     reduce-scatter (default: on when the group has > 1 rank)
     average_grads   divide the summed gradient by the group size (default on)
+    bucket_elems    elements per pipelined bucket (rounded to N*64)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -77,11 +83,13 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  weight_decay: float = 0.0, enable_fiber: bool = True, *,
                  moment_format: str = "packed", process_group=None,
                  compress_grads: bool | None = None, average_grads: bool = True,
-                 backend=None):
+                 bucket_elems: int = DEFAULT_BUCKET, backend=None):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
             raise ValueError(f"moment_format must be one of {_FORMATS}")
+        if bucket_elems <= 0:
+            raise ValueError("bucket_elems must be positive")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
         self.enable_fiber = bool(enable_fiber)
         self.moment_format = moment_format
@@ -91,11 +99,11 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.compress = (self.world > 1) if compress_grads is None else bool(compress_grads)
         self.average = bool(average_grads)
         self.kernels = backend if backend is not None else CudaKernels()
-        self._layout()
+        self._layout(bucket_elems)
 
     # ---- layout -----------------------------------------------------------
     @torch.no_grad()
-    def _layout(self):
+    def _layout(self, bucket_elems: int):
         self.params = [p for g in self.param_groups for p in g["params"]]
         self.group_of = [gi for gi, g in enumerate(self.param_groups) for _ in g["params"]]
         if not self.params:
@@ -107,13 +115,18 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             if p.device != dev:
                 raise RuntimeError("all parameters must live on one device")
         self.device = dev
-        offs, o = [], 0
+        offs, total = [], 0
         for p in self.params:
-            offs.append(o)
-            o += -(-p.numel() // PARAM_ALIGN) * PARAM_ALIGN
+            offs.append(total)
+            total += -(-p.numel() // PARAM_ALIGN) * PARAM_ALIGN
         n = self.world
-        self.shard = -(-o // (n * SHARD_ALIGN)) * SHARD_ALIGN
-        self.padded = self.shard * n
+        unit = n * PIECE_ALIGN
+        whole = -(-total // unit) * unit
+        bucket = min(max(unit, bucket_elems // unit * unit), whole)
+        self.bucket = bucket
+        self.piece = bucket // n
+        self.n_buckets = -(-total // bucket)
+        self.padded = self.n_buckets * bucket
         self.offsets = offs
         self.flat_param = torch.zeros(self.padded, dtype=torch.float32, device=dev)
         self.flat_grad = torch.zeros(self.padded, dtype=torch.float32, device=dev)
@@ -122,32 +135,49 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             self.flat_param[off:off + k].copy_(p.detach().reshape(-1))
             p.data = self.flat_param[off:off + k].view_as(p)
             p.grad = self.flat_grad[off:off + k].view_as(p)
-        lo = self.rank * self.shard
-        self.shard_range = (lo, lo + self.shard)
+        local = self.n_buckets * self.piece
         if self.compress:
             self.comp = torch.zeros(self.padded, dtype=torch.int16, device=dev)
             self.resid = torch.zeros(self.padded, dtype=torch.int16, device=dev)
-            self.shard_grad = torch.zeros(self.shard, dtype=torch.bfloat16, device=dev)
+            self.shard_grad = torch.zeros(local, dtype=torch.bfloat16, device=dev)
         elif n > 1:
-            self.shard_grad = torch.zeros(self.shard, dtype=torch.float32, device=dev)
+            self.shard_grad = torch.zeros(local, dtype=torch.float32, device=dev)
         else:
             self.shard_grad = self.flat_grad
-        self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        self.exp_avg_sq = torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        # one segment per parameter slice that falls inside this shard
-        self.segments, self.seg_param = [], []
-        for i, (p, off) in enumerate(zip(self.params, offs)):
-            a, b = max(off, lo), min(off + p.numel(), lo + self.shard)
-            if a >= b:
-                continue
-            s = a - lo
-            g = self.shard_grad[s:s + b - a] if self.shard_grad is not self.flat_grad \
-                else self.flat_grad[a:b]
-            self.segments.append((self.flat_param[a:b], g, self.exp_avg[s:s + b - a],
-                                  self.exp_avg_sq[s:s + b - a]))
-            self.seg_param.append(i)
+        self.exp_avg = torch.zeros(local, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(local, dtype=torch.float32, device=dev)
+        # per bucket: the parameter slices that fall in this rank's piece
+        self.bucket_segments, self.bucket_params = [], []
+        for b in range(self.n_buckets):
+            lo = b * bucket + self.rank * self.piece   # flat range this rank owns
+            base = b * self.piece                      # where it lives locally
+            segs, pidx = [], []
+            for i, (p, off) in enumerate(zip(self.params, offs)):
+                a, e = max(off, lo), min(off + p.numel(), lo + self.piece)
+                if a >= e:
+                    continue
+                s = base + a - lo
+                g = self.flat_grad[a:e] if self.shard_grad is self.flat_grad \
+                    else self.shard_grad[s:s + e - a]
+                segs.append((self.flat_param[a:e], g, self.exp_avg[s:s + e - a],
+                             self.exp_avg_sq[s:s + e - a]))
+                pidx.append(i)
+            self.bucket_segments.append(segs)
+            self.bucket_params.append(pidx)
         for p in self.params:
             self.state[p]["step"] = 0
+
+    def _bucket(self, t: torch.Tensor, b: int) -> torch.Tensor:
+        return t[b * self.bucket:(b + 1) * self.bucket]
+
+    def _piece(self, t: torch.Tensor, b: int) -> torch.Tensor:
+        """This rank's piece of bucket b inside a full-length flat tensor."""
+        lo = b * self.bucket + self.rank * self.piece
+        return t[lo:lo + self.piece]
+
+    def _local(self, t: torch.Tensor, b: int) -> torch.Tensor:
+        """Bucket b's slot in a local (per-rank) tensor."""
+        return t[b * self.piece:(b + 1) * self.piece]
 
     @property
     def mode(self) -> int:
@@ -162,13 +192,13 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
 
     # ---- reference-compatible surface --------------------------------------
     def second_moment_tensors(self) -> list[torch.Tensor]:
-        """Second-moment words of this rank's shard, one view per parameter
+        """Second-moment words of this rank's pieces, one view per parameter
         slice (alignment padding excluded): this rank's sign fiber."""
-        return [v for _, _, _, v in self.segments]
+        return [v for segs in self.bucket_segments for _, _, _, v in segs]
 
     @property
     def payload_bit_capacity(self) -> int:
-        return sum(v.numel() for _, _, _, v in self.segments) if self.enable_fiber else 0
+        return sum(v.numel() for v in self.second_moment_tensors()) if self.enable_fiber else 0
 
     @torch.no_grad()
     def zero_grad(self, set_to_none: bool = False):
@@ -184,37 +214,58 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 loss = closure()
         self._check_grads()
         n = self.world
-        if self.compress:
-            self.kernels.compress_ef(self.flat_grad, self.comp, self.resid)
-            if n > 1:
-                dist.reduce_scatter_tensor(self.shard_grad, self.comp.view(torch.bfloat16),
-                                           op=dist.ReduceOp.SUM, group=self.group)
-            else:
-                self.shard_grad.copy_(self.comp.view(torch.bfloat16))
-        elif n > 1:
-            dist.reduce_scatter_tensor(self.shard_grad, self.flat_grad, op=dist.ReduceOp.SUM,
-                                       group=self.group)
         scale = 1.0 / n if (self.average and n > 1) else 1.0
-        rows, index, seen = [], [], {}
         steps = []
-        for p, gi in zip(self.params, self.group_of):
+        for p in self.params:
             st = self.state[p]
             st["step"] += 1
             steps.append(st["step"])
-        for pi in self.seg_param:
-            k = (self.group_of[pi], steps[pi])
-            j = seen.get(k)
-            if j is None:
-                g = self.param_groups[k[0]]
-                j = seen[k] = len(rows)
-                rows.append(hyper_row(g["lr"], g["betas"], g["eps"], g["weight_decay"], k[1],
-                                      grad_scale=scale))
-            index.append(j)
-        if self.segments:
-            self.kernels.step(self.segments, rows, index, self.mode, self.device)
-        if n > 1:
-            lo, hi = self.shard_range
-            dist.all_gather_into_tensor(self.flat_param, self.flat_param[lo:hi], group=self.group)
+        rows, seen = [], {}
+        index = []
+        for pidx in self.bucket_params:
+            idx = []
+            for pi in pidx:
+                k = (self.group_of[pi], steps[pi])
+                j = seen.get(k)
+                if j is None:
+                    g = self.param_groups[k[0]]
+                    j = seen[k] = len(rows)
+                    rows.append(hyper_row(g["lr"], g["betas"], g["eps"], g["weight_decay"], k[1],
+                                          grad_scale=scale))
+                idx.append(j)
+            index.append(idx)
+
+        def reduce(b):
+            if self.compress:
+                self.kernels.compress_ef(self._bucket(self.flat_grad, b),
+                                         self._bucket(self.comp, b), self._bucket(self.resid, b))
+                if n == 1:
+                    self._local(self.shard_grad, b).copy_(self._bucket(self.comp, b).view(torch.bfloat16))
+                    return None
+                src = self._bucket(self.comp, b).view(torch.bfloat16)
+            elif n > 1:
+                src = self._bucket(self.flat_grad, b)
+            else:
+                return None
+            return dist.reduce_scatter_tensor(self._local(self.shard_grad, b), src,
+                                              op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+
+        gathers = []
+        pending = reduce(0)
+        for b in range(self.n_buckets):
+            nxt = reduce(b + 1) if b + 1 < self.n_buckets else None
+            if pending is not None:
+                pending.wait()
+            if self.bucket_segments[b]:
+                self.kernels.step(self.bucket_segments[b], rows, index[b], self.mode, self.device,
+                                  key=b)
+            if n > 1:
+                gathers.append(dist.all_gather_into_tensor(
+                    self._bucket(self.flat_param, b), self._piece(self.flat_param, b),
+                    group=self.group, async_op=True))
+            pending = nxt
+        for w in gathers:
+            w.wait()
         return loss
 
     def _check_grads(self):
@@ -226,12 +277,28 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 raise RuntimeError("ShardedDFCAdamW owns .grad of its parameters; use its "
                                    "zero_grad() (set_to_none is not supported)")
 
+    @torch.no_grad()
+    def full_reduced_grad(self) -> torch.Tensor:
+        """The gradient the last step used, in flat order on every rank
+        (collective; for checking and debugging)."""
+        out = torch.empty(self.padded, dtype=self.shard_grad.dtype, device=self.device)
+        if self.world == 1:
+            return out.copy_(self.shard_grad[:self.padded])
+        for b in range(self.n_buckets):
+            dist.all_gather_into_tensor(self._bucket(out, b), self._local(self.shard_grad, b),
+                                        group=self.group)
+        return out
+
     # ---- checkpoints -------------------------------------------------------
+    def _layout_info(self):
+        return {"rank": self.rank, "world": self.world, "bucket": self.bucket,
+                "padded": self.padded}
+
     def state_dict(self):
-        """This rank's shard (moment words, step counters, layout)."""
+        """This rank's pieces (moment words, step counters, layout)."""
         return {
             "shard": {"exp_avg": self.exp_avg.clone(), "exp_avg_sq": self.exp_avg_sq.clone(),
-                      "rank": self.rank, "world": self.world, "shard": self.shard},
+                      **self._layout_info()},
             "steps": [self.state[p]["step"] for p in self.params],
             "param_groups": [{k: v for k, v in g.items() if k != "params"}
                              for g in self.param_groups],
@@ -241,7 +308,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def load_state_dict(self, state_dict):
         sh = state_dict["shard"]
-        if sh["world"] != self.world or sh["shard"] != self.shard or sh["rank"] != self.rank:
+        if any(sh[k] != v for k, v in self._layout_info().items()):
             raise ValueError("shard layout differs; use load_consolidated_state_dict")
         self.exp_avg.copy_(sh["exp_avg"])
         self.exp_avg_sq.copy_(sh["exp_avg_sq"])
@@ -263,16 +330,19 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     def consolidated_state_dict(self, to_rank: int | None = 0):
         """The whole optimizer state in DFCAdamW's per-parameter layout
         (``state[i] = {step, exp_avg, exp_avg_sq}``), gathered from every
-        shard.  Collective: every rank must call it.  Returns the dict on
+        rank.  Collective: every rank must call it.  Returns the dict on
         ``to_rank`` (every rank when None), else None."""
         full_m = torch.empty(self.padded, dtype=torch.float32, device=self.device)
         full_v = torch.empty(self.padded, dtype=torch.float32, device=self.device)
-        if self.world > 1:
-            dist.all_gather_into_tensor(full_m, self.exp_avg, group=self.group)
-            dist.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.group)
-        else:
-            full_m.copy_(self.exp_avg)
-            full_v.copy_(self.exp_avg_sq)
+        for b in range(self.n_buckets):
+            if self.world > 1:
+                dist.all_gather_into_tensor(self._bucket(full_m, b), self._local(self.exp_avg, b),
+                                            group=self.group)
+                dist.all_gather_into_tensor(self._bucket(full_v, b),
+                                            self._local(self.exp_avg_sq, b), group=self.group)
+            else:
+                self._bucket(full_m, b).copy_(self._local(self.exp_avg, b))
+                self._bucket(full_v, b).copy_(self._local(self.exp_avg_sq, b))
         if to_rank is not None and self.rank != to_rank:
             return None
         state, groups, idx = {}, [], 0
@@ -291,9 +361,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def load_consolidated_state_dict(self, state_dict):
         """Load a per-parameter state dict (this class's consolidated form,
-        DFCAdamW's, or the reference's) and keep this rank's shard."""
+        DFCAdamW's, or the reference's) and keep this rank's pieces."""
         st = state_dict["state"]
-        lo, hi = self.shard_range
         flat_m = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
         flat_v = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
         for i, (p, off) in enumerate(zip(self.params, self.offsets)):
@@ -304,8 +373,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             flat_m[off:off + k].copy_(s["exp_avg"].reshape(-1))
             flat_v[off:off + k].copy_(s["exp_avg_sq"].reshape(-1))
             self.state[p]["step"] = int(s["step"])
-        self.exp_avg.copy_(flat_m[lo:hi])
-        self.exp_avg_sq.copy_(flat_v[lo:hi])
+        for b in range(self.n_buckets):
+            self._local(self.exp_avg, b).copy_(self._piece(flat_m, b))
+            self._local(self.exp_avg_sq, b).copy_(self._piece(flat_v, b))
         for g, saved in zip(self.param_groups, state_dict["param_groups"]):
             g.update({k: v for k, v in saved.items() if k != "params"})
         self._convert_from(state_dict.get("moment_format", "fp32"))

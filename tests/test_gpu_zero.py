@@ -1,0 +1,131 @@
+"""ZeRO-1 ShardedDFCAdamW on CUDA: one GPU (no collective), and two GPUs
+over NCCL when the machine has them (the bf16 reduce-scatter result is read
+back from every shard and the step is checked bit for bit against the oracle
+given that reduced gradient)."""
+
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(257, 31), (31,), (4099,), (3, 3, 3), (1 << 16,)]
+
+
+def _grads(rank, step, sizes):
+    rng = np.random.default_rng(1000 * step + rank)
+    return [(rng.standard_normal(n) * 1e-3).astype(np.float32) for n in sizes]
+
+
+def _run(rank, world, device, compress):
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter((torch.randn(s) * 0.02).to(device)) for s in SHAPES]
+    sizes = [p.numel() for p in params]
+    p0 = [p.detach().cpu().numpy().reshape(-1).copy() for p in params]
+    opt = ShardedDFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed",
+                          compress_grads=compress, bucket_elems=8192)
+    sim_p = [x.copy() for x in p0]
+    sim_m = [np.zeros(n, np.uint32) for n in sizes]
+    sim_v = [np.zeros(n, np.uint32) for n in sizes]
+    ef_c = [np.zeros(opt.padded, np.uint16) for _ in range(world)]
+    ef_q = [np.zeros(opt.padded, np.uint16) for _ in range(world)]
+    for step in range(1, 6):
+        opt.zero_grad()
+        for p, g in zip(params, _grads(rank, step, sizes)):
+            p.grad.copy_(torch.from_numpy(g).view_as(p))
+        opt.step()
+        torch.cuda.synchronize()
+        if world > 1:
+            red16 = opt.full_reduced_grad().view(torch.int16).cpu().numpy().view(np.uint16)
+            gsrc = [red16[off:off + n].copy() for off, n in zip(opt.offsets, sizes)]
+            scale = 1.0 / world
+        elif compress:
+            flat = np.zeros(opt.padded, np.float32)
+            for off, g in zip(opt.offsets, _grads(rank, step, sizes)):
+                flat[off:off + g.size] = g
+            O.compress_ef(flat, ef_c[0], ef_q[0])
+            gsrc = [ef_c[0][off:off + n].copy() for off, n in zip(opt.offsets, sizes)]
+            scale = 1.0
+        else:
+            gsrc = _grads(rank, step, sizes)
+            scale = 1.0
+        h = O.reference_hyper(1e-3, (0.9, 0.999), 1e-8, 0.01, step, grad_scale=scale)
+        for i in range(len(sizes)):
+            O.step(O.MODE_PACKED, h, sim_p[i], gsrc[i], sim_m[i], sim_v[i])
+        for i, p in enumerate(params):
+            np.testing.assert_array_equal(p.detach().cpu().numpy().reshape(-1).view(np.uint32),
+                                          sim_p[i].view(np.uint32))
+    full = opt.consolidated_state_dict(to_rank=None)
+    for i in range(len(sizes)):
+        np.testing.assert_array_equal(full["state"][i]["exp_avg"].cpu().numpy().reshape(-1).view(np.uint32), sim_m[i])
+        np.testing.assert_array_equal(full["state"][i]["exp_avg_sq"].cpu().numpy().reshape(-1).view(np.uint32), sim_v[i])
+    return opt, params
+
+
+@pytest.mark.parametrize("compress", [False, True])
+def test_sharded_on_one_gpu_matches_oracle(cuda, compress):
+    opt, params = _run(0, 1, cuda, compress)
+    # the consolidated state loads into the single-GPU DFCAdamW
+    from t3st_b200 import DFCAdamW
+
+    single = DFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed")
+    single.load_state_dict(opt.consolidated_state_dict())
+    for i, p in enumerate(params):
+        assert single.state[p]["step"] == 5
+        full = opt.consolidated_state_dict()["state"][i]["exp_avg"]
+        assert torch.equal(single.state[p]["exp_avg"].view(torch.int32), full.view(torch.int32))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        _run(rank, world, dev, True)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except BaseException:
+        q.put((rank, traceback.format_exc()))
+
+
+def test_sharded_on_two_gpus_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert results[r] == "ok", results[r]

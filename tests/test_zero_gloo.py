@@ -23,7 +23,7 @@ class OracleBackend:
     def compress_ef(self, g, c, q):
         O.compress_ef(g.numpy(), c.numpy().view(np.uint16), q.numpy().view(np.uint16))
 
-    def step(self, segments, rows, index, mode, device):
+    def step(self, segments, rows, index, mode, device, key=0):
         for (p, g, m, v), j in zip(segments, index):
             h = O.Hyper(*rows[j][:9])
             gg = g.view(torch.int16).numpy().view(np.uint16) if g.dtype == torch.bfloat16 else g.numpy()
@@ -68,7 +68,8 @@ def _worker(rank, world, port, fmt, result_q):
         p0 = [p.detach().numpy().reshape(-1).copy() for p in params]
         groups = [{"params": params[:3]}, {"params": params[3:], "lr": 3e-4, "weight_decay": 0.0}]
         opt = ShardedDFCAdamW(groups, lr=1e-3, weight_decay=0.01, moment_format=fmt,
-                              backend=OracleBackend())
+                              backend=OracleBackend(), bucket_elems=256)
+        assert opt.n_buckets >= 4
         sizes = [p.numel() for p in params]
         # payload in this rank's fiber (the shard's real coordinates)
         prng = np.random.default_rng(rank)
@@ -93,8 +94,7 @@ def _worker(rank, world, port, fmt, result_q):
                 p.grad.copy_(torch.from_numpy(g).view_as(p))
             opt.step()
             # gather the reduced gradient the step used, from every shard
-            red = torch.empty(opt.padded, dtype=torch.bfloat16)
-            dist.all_gather_into_tensor(red, opt.shard_grad)
+            red = opt.full_reduced_grad()
             red16 = red.view(torch.int16).numpy().view(np.uint16).copy()
             exact = np.zeros(opt.padded, np.float64)
             mag = np.zeros(opt.padded, np.float64)
@@ -131,11 +131,12 @@ def _worker(rank, world, port, fmt, result_q):
         # round trip through a fresh optimizer, including a format change
         params2 = [torch.nn.Parameter(p.detach().clone()) for p in params]
         other = "fp32" if fmt == "packed" else "packed"
-        opt2 = ShardedDFCAdamW(params2, moment_format=other, backend=OracleBackend())
+        opt2 = ShardedDFCAdamW(params2, moment_format=other, backend=OracleBackend(),
+                               bucket_elems=4096)
         opt2.load_consolidated_state_dict(full)
         back = opt2.consolidated_state_dict(to_rank=None)
         opt3 = ShardedDFCAdamW([torch.nn.Parameter(p.detach().clone()) for p in params],
-                               moment_format=fmt, backend=OracleBackend())
+                               moment_format=fmt, backend=OracleBackend(), bucket_elems=256)
         opt3.load_consolidated_state_dict(back)
         assert torch.equal(opt3.exp_avg.view(torch.int32), opt.exp_avg.view(torch.int32))
         assert torch.equal(opt3.exp_avg_sq.view(torch.int32), opt.exp_avg_sq.view(torch.int32))
