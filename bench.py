@@ -58,6 +58,8 @@ def parse_args():
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-clocks", action="store_true",
                     help="skip the nvidia-smi clock sampler (profiling runs)")
+    ap.add_argument("--no-host-overhead", action="store_true",
+                    help="skip the host-overhead measurement (profiling runs)")
     return ap.parse_args()
 
 
@@ -385,7 +387,8 @@ def run_single(args, device):
         "host_wall_ms_per_step": wall / K * 1e3,
     }
 
-    line["host_us_per_step"] = host_overhead_us(opt)
+    if not args.no_host_overhead:
+        line["host_us_per_step"] = host_overhead_us(opt)
     if not args.no_e2e:
         line["e2e"] = run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K)
     if not args.no_cpu_baseline:
