@@ -45,14 +45,10 @@ namespace {
 #ifndef DFC_STEP_MIN_BLOCKS
 #define DFC_STEP_MIN_BLOCKS 8
 #endif
-#ifndef DFC_STEP_ITERS
-#define DFC_STEP_ITERS 1
-#endif
 constexpr int kThreads = DFC_STEP_THREADS;
 constexpr int kVec = 4;
 constexpr int kUnroll = DFC_STEP_UNROLL;
-constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA iteration
-constexpr int kIters = DFC_STEP_ITERS;             // consecutive tiles per CTA
+constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA
 
 constexpr int32_t kFlagBf16 = 1;
 constexpr int32_t kFlagVec = 2;
@@ -200,45 +196,35 @@ __device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int
 template <int MODE, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, DFC_STEP_MIN_BLOCKS)
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
-  // This CTA walks tiles [t, t_end) in order; the tiles of one segment are
-  // consecutive, so the segment search runs once and then only steps forward.
-  const int32_t total = b.tile_base[b.n_segs];
-  int32_t t = static_cast<int32_t>(blockIdx.x) * kIters;
-  const int32_t t_end = min(t + kIters, total);
-  int seg = 0, hi = b.n_segs;  // tile_base[seg] <= t < tile_base[hi]
-  while (hi - seg > 1) {
-    const int mid = (seg + hi) >> 1;
-    if (b.tile_base[mid] <= t) seg = mid; else hi = mid;
+  const int32_t t = static_cast<int32_t>(blockIdx.x);
+  int lo = 0, hi = b.n_segs;  // tile_base[lo] <= t < tile_base[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
   }
-  const float dscale = b.dev_scale ? *b.dev_scale : 1.0f;
-  for (; t < t_end; ++seg) {
-    const SegArg& sg = b.seg[seg];
-    const DfcHyper& h = b.hyper[sg.hyper];
-    Scalars s;
-    s.b1 = h.beta1;
-    s.omb1 = h.one_minus_beta1;
-    s.b2 = h.beta2;
-    s.omb2 = h.one_minus_beta2;
-    s.sbc2 = h.sqrt_bc2;
-    s.eps = h.eps;
-    s.decay = h.decay;
-    s.nstep = h.neg_step_size;
-    s.gscale = h.grad_scale;
-    s.dscale = dscale;
-    const bool vec = (sg.flags & kFlagVec) != 0;
-    const bool bf16 = (sg.flags & kFlagBf16) != 0;
-    const int32_t seg_end = min(b.tile_base[seg + 1], t_end);
-    for (; t < seg_end; ++t) {
-      const int64_t base = static_cast<int64_t>(t - b.tile_base[seg]) * kTile;
-      const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
-      if (bf16) {
-        if (vec && count == kTile) tile_full_vec<MODE, true>(sg, base, s);
-        else tile_partial<MODE, true>(sg, base, count, vec, s);
-      } else {
-        if (vec && count == kTile) tile_full_vec<MODE, false>(sg, base, s);
-        else tile_partial<MODE, false>(sg, base, count, vec, s);
-      }
-    }
+  const SegArg& sg = b.seg[lo];
+  const DfcHyper& h = b.hyper[sg.hyper];
+  Scalars s;
+  s.b1 = h.beta1;
+  s.omb1 = h.one_minus_beta1;
+  s.b2 = h.beta2;
+  s.omb2 = h.one_minus_beta2;
+  s.sbc2 = h.sqrt_bc2;
+  s.eps = h.eps;
+  s.decay = h.decay;
+  s.nstep = h.neg_step_size;
+  s.gscale = h.grad_scale;
+  s.dscale = b.dev_scale ? *b.dev_scale : 1.0f;
+
+  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+  const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
+  const bool vec = (sg.flags & kFlagVec) != 0;
+  if (sg.flags & kFlagBf16) {
+    if (vec && count == kTile) tile_full_vec<MODE, true>(sg, base, s);
+    else tile_partial<MODE, true>(sg, base, count, vec, s);
+  } else {
+    if (vec && count == kTile) tile_full_vec<MODE, false>(sg, base, s);
+    else tile_partial<MODE, false>(sg, base, count, vec, s);
   }
 }
 
@@ -246,7 +232,7 @@ template <int MAXS, int MAXH>
 int launch_batch(StepBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
   const int32_t tiles = b.tile_base[b.n_segs];
   if (tiles == 0) return DFC_OK;
-  const int32_t grid = (tiles + kIters - 1) / kIters;
+  const int32_t grid = tiles;
   switch (mode) {
     case DFC_MODE_PLAIN:
       step_kernel<DFC_MODE_PLAIN, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b);

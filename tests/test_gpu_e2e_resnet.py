@@ -1,27 +1,40 @@
 """End-to-end training parity: ResNet-18 (3x3 stem, no max-pool, 10
-classes) on a fixed synthetic batch of 256 N(0,1) 3x32x32 images with
-uniform int64 labels, bf16 autocast forward/backward, cross-entropy.
+classes), batches of 256 N(0,1) 3x32x32 images with uniform int64 labels,
+bf16 autocast forward/backward, cross-entropy, deterministic algorithms.
 
-Three runs from the same initial weights, 200 steps each:
-  reference   the reference's FP32 DFCAdamW step (remote/torch_fiber.py:
-              68-117, fiber on) restated as eager PyTorch ops on the GPU
-  packed      t3st_b200 DFCAdamW, packed moment words, FP32 gradients
-  compressed  t3st_b200 ShardedDFCAdamW on one GPU: bf16 gradients with
-              per-element error feedback, packed moments
-The loss curves must agree with the reference's to 1e-3 relative over the
-first 100 steps."""
+The reference optimizer is the reference's FP32 DFCAdamW step
+(remote/torch_fiber.py:68-117, fiber on) run by the oracle on the host each
+step (the reference's CPU arithmetic, with an IEEE square root): gradients
+go to the host, the oracle updates p, m, v there, p comes back.
+
+  * t3st_b200 DFCAdamW with packed moment words and FP32 gradients must
+    reproduce the reference's loss curve exactly, every step (fixed batch,
+    so the loss falls and the run is sensitive to any difference).
+  * ShardedDFCAdamW on one GPU with bf16 error-feedback gradients must stay
+    within 1e-3 relative of the reference's loss curve over 100 steps
+    (a fresh seeded batch every step).
+"""
 
 import numpy as np
 import pytest
 import torch
 
-from oracle import torch_port
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-STEPS = 200
-CHECK = 100
 LR, BETAS, EPS, WD = 1e-3, (0.9, 0.999), 1e-8, 0.01
+
+
+@pytest.fixture
+def deterministic():
+    prev = torch.are_deterministic_algorithms_enabled()
+    prev_cudnn = (torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark)
+    torch.use_deterministic_algorithms(True)
+    torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark = True, False
+    yield
+    torch.use_deterministic_algorithms(prev)
+    torch.backends.cudnn.deterministic, torch.backends.cudnn.benchmark = prev_cudnn
 
 
 def _model(device):
@@ -33,11 +46,15 @@ def _model(device):
     return m.to(device)
 
 
-def _batch(device):
+def _batches(device, fresh):
     g = torch.Generator().manual_seed(1)
-    x = torch.randn(256, 3, 32, 32, generator=g).to(device)
-    y = torch.randint(0, 10, (256,), generator=g).to(device)
-    return x, y
+    while True:
+        x = torch.randn(256, 3, 32, 32, generator=g).to(device)
+        y = torch.randint(0, 10, (256,), generator=g).to(device)
+        while True:
+            yield x, y
+            if fresh:
+                break
 
 
 def _loss(model, x, y):
@@ -46,22 +63,30 @@ def _loss(model, x, y):
     return torch.nn.functional.cross_entropy(out.float(), y)
 
 
-def _train(kind, device, init, x, y):
+def _train(kind, device, init, steps, fresh):
     model = _model(device)
     model.load_state_dict(init)
     params = list(model.parameters())
+    data = _batches(device, fresh)
     losses = []
     if kind == "reference":
-        state = [(torch.zeros_like(p), torch.zeros_like(p)) for p in params]
-        for t in range(1, STEPS + 1):
+        host = [dict(p=p.detach().cpu().numpy().reshape(-1).copy(),
+                     m=np.zeros(p.numel(), np.uint32), v=np.zeros(p.numel(), np.uint32))
+                for p in params]
+        counters = [0] * len(params)
+        group = dict(lr=LR, betas=BETAS, eps=EPS, weight_decay=WD)
+        for _ in range(steps):
+            x, y = next(data)
             for p in params:
                 p.grad = None
             loss = _loss(model, x, y)
             loss.backward()
             losses.append(loss.item())
+            grads = [p.grad.detach().cpu().numpy().reshape(-1) for p in params]
+            O.multi_tensor_step(O.MODE_SIGNFIBER, host, grads, group, counters)
             with torch.no_grad():
-                for p, (m, v) in zip(params, state):
-                    torch_port.step_fp32(p.data, p.grad, m, v, LR, BETAS, EPS, WD, t, fiber=True)
+                for p, h in zip(params, host):
+                    p.copy_(torch.from_numpy(h["p"]).view_as(p))
         return np.array(losses)
     if kind == "packed":
         from t3st_b200 import DFCAdamW
@@ -73,7 +98,8 @@ def _train(kind, device, init, x, y):
 
         opt = ShardedDFCAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
                               moment_format="packed", compress_grads=True)
-    for _ in range(STEPS):
+    for _ in range(steps):
+        x, y = next(data)
         opt.zero_grad()
         loss = _loss(model, x, y)
         loss.backward()
@@ -82,14 +108,17 @@ def _train(kind, device, init, x, y):
     return np.array(losses)
 
 
-def test_resnet18_loss_curves_match_reference(cuda):
-    torch.backends.cudnn.deterministic = True
-    torch.backends.cudnn.benchmark = False
+def test_packed_step_reproduces_reference_loss_curve_exactly(cuda, deterministic):
     init = {k: v.clone() for k, v in _model(cuda).state_dict().items()}
-    x, y = _batch(cuda)
-    ref = _train("reference", cuda, init, x, y)
-    assert ref[CHECK - 1] < 0.9 * ref[0]  # the run actually trains
-    for kind in ("packed", "compressed"):
-        got = _train(kind, cuda, init, x, y)
-        rel = np.abs(got[:CHECK] - ref[:CHECK]) / np.abs(ref[:CHECK])
-        assert rel.max() <= 1e-3, (kind, float(rel.max()), int(rel.argmax()))
+    ref = _train("reference", cuda, init, 100, fresh=False)
+    assert ref[-1] < 0.5 * ref[0]  # the fixed batch is being learned
+    got = _train("packed", cuda, init, 100, fresh=False)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_compressed_grads_loss_curve_within_1e3(cuda, deterministic):
+    init = {k: v.clone() for k, v in _model(cuda).state_dict().items()}
+    ref = _train("reference", cuda, init, 100, fresh=True)
+    got = _train("compressed", cuda, init, 100, fresh=True)
+    rel = np.abs(got - ref) / np.abs(ref)
+    assert rel.max() <= 1e-3, (float(rel.max()), int(rel.argmax()))
