@@ -60,6 +60,8 @@ def parse_args():
                     help="skip the nvidia-smi clock sampler (profiling runs)")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
+    ap.add_argument("--transport", choices=("peer", "nccl"), default="peer",
+                    help="N>1: fused kernel over NVLink peer memory, or NCCL collectives")
     return ap.parse_args()
 
 
@@ -474,7 +476,7 @@ def run_sharded(args, rank, world, device):
     gen = torch.Generator(device=device).manual_seed(1234)  # same params on every rank
     param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
     opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
-                          moment_format="packed")
+                          moment_format="packed", transport=args.transport)
     del param
     ggen = torch.Generator(device=device).manual_seed(100 + rank)  # per-rank gradients
     opt.flat_grad[:P].normal_(0.0, 1e-3, generator=ggen)
@@ -512,10 +514,13 @@ def run_sharded(args, rank, world, device):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {
                 "workload": "ZeRO-1 sharded DFC-AdamW step over a flat 2^30-element FP32 "
-                            "parameter vector: bf16 error-feedback compression, NCCL "
-                            "reduce-scatter, fused packed-moment step on the 1/N shard, "
-                            "NCCL FP32 all-gather",
+                            "parameter vector: bf16 error-feedback compression, reduce of "
+                            "the bf16 gradients, packed-moment step on the rank's 1/N, FP32 "
+                            "parameter broadcast (peer: one fused kernel over NVLink peer "
+                            "memory between two barriers; nccl: reduce-scatter + step + "
+                            "all-gather)",
                 "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
+                "transport": args.transport,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
             },
             "roofline": {"bound": "nvlink" if t_nvl > t_hbm else "hbm",
@@ -524,7 +529,7 @@ def run_sharded(args, rank, world, device):
                          "hbm_bytes_per_rank": hbm_bytes, "nvlink_bytes_per_rank": nvl_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": f"{peak_kind} hbm_gbs",
                          "nvlink_gbs": NVLINK_GBS, "traffic": None},
-            "gpu_launches": K * 2,
+            "gpu_launches": K * (4 if args.transport == "peer" else 2 * opt.n_buckets),
             "clocks": clocks,
         }
     if not args.no_e2e:

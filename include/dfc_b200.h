@@ -117,6 +117,19 @@ typedef struct DfcGradStats {
   int64_t nonfinite;   /* number of Inf/NaN elements */
 } DfcGradStats;
 
+/* Most ranks a fused ZeRO-1 call can span. */
+#define DFC_MAX_PEERS 8
+
+/* One run of this rank's elements for dfc_zero_fused_step.  40 bytes. */
+typedef struct DfcPeerSegment {
+  int64_t offset;        /* flat element index into every rank's comp and param arrays */
+  int64_t numel;
+  uint32_t* exp_avg;     /* this rank's first-moment words for the run */
+  uint32_t* exp_avg_sq;  /* this rank's second-moment words for the run */
+  int32_t hyper;         /* index into the call's DfcHyper array */
+  int32_t reserved;
+} DfcPeerSegment;
+
 /* A run of second-moment words whose bit 31 forms part of the sign fiber. */
 typedef struct DfcWordRange {
   uint32_t* words;
@@ -218,6 +231,38 @@ DFC_API int dfc_fiber_read(const DfcWordRange* ranges, int32_t n_ranges, int64_t
                    int64_t n_bits, uint8_t* bytes, void* stream);
 DFC_API int dfc_fiber_write(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
                     int64_t n_bits, const uint8_t* bytes, void* stream);
+
+/*
+ * ZeRO-1 shard step fused with its collectives over NVLink peer memory (no
+ * counterpart in the reference, which has no distributed code; replaces
+ * NCCL reduce-scatter + dfc_mt_step + NCCL all-gather).  comp_ptrs and
+ * param_ptrs are host arrays of n_peers DEVICE addresses, indexed by rank, of
+ * every rank's bf16 compressed gradients and flat FP32 parameters, all
+ * mapped into this process (symmetric memory); 16-byte aligned.  For every
+ * element j of the segments: g = comp_0[j] + comp_1[j] + ... (FP32, rank
+ * order), the DFC-AdamW step on this rank's moment words, then the new
+ * parameter stored to param_q[j] of every rank q.  The caller brackets the
+ * call with dfc_peer_barrier: before it so every rank's gradients are
+ * complete, after it so every rank's parameters are.
+ */
+DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
+                                int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
+                                int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
+                                int32_t mode, const float* device_grad_scale, void* stream);
+
+/*
+ * Barrier across ranks on their streams.  slot_ptrs: host array of n_peers
+ * device addresses of every rank's uint32 signal array (n_peers words each,
+ * peer-mapped, zero before the first use).  Rank r stores `epoch` into word
+ * r of every array (release, system scope), then waits until every word of
+ * its own array has reached `epoch` (acquire, system scope), for at most
+ * timeout_ns; on time-out it stores 1 + the index of the missing rank into
+ * *error_flag (device int) and returns.  Epochs must increase by one per
+ * call.  One rank per GPU: ranks sharing a GPU may never run concurrently.
+ */
+DFC_API int dfc_peer_barrier(uint32_t* const* slot_ptrs, int32_t n_peers, int32_t rank,
+                             uint32_t epoch, int32_t* error_flag, int64_t timeout_ns,
+                             void* stream);
 
 #ifdef __cplusplus
 }

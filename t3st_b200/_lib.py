@@ -51,9 +51,12 @@ GRADREF_DTYPE = np.dtype([("grad", "<u8"), ("numel", "<i8"), ("grad_dtype", "<i4
 GRADSTATS_DTYPE = np.dtype([("sumsq", "<f8"), ("amax", "<f4"), ("reserved", "<i4"),
                             ("nonfinite", "<i8")])
 WORDRANGE_DTYPE = np.dtype([("words", "<u8"), ("count", "<i8")])
+PEERSEG_DTYPE = np.dtype([("offset", "<i8"), ("numel", "<i8"), ("exp_avg", "<u8"),
+                          ("exp_avg_sq", "<u8"), ("hyper", "<i4"), ("reserved", "<i4")])
+MAX_PEERS = 8
 assert SEGMENT_DTYPE.itemsize == 48 and HYPER_DTYPE.itemsize == 48
 assert GRADREF_DTYPE.itemsize == 24 and GRADSTATS_DTYPE.itemsize == 24
-assert WORDRANGE_DTYPE.itemsize == 16
+assert WORDRANGE_DTYPE.itemsize == 16 and PEERSEG_DTYPE.itemsize == 40
 
 # Names of every entry point the header declares (checked by the CPU tests).
 EXPORTS = (
@@ -61,6 +64,7 @@ EXPORTS = (
     "dfc_pack_moments", "dfc_unpack_moments", "dfc_compress_ef",
     "dfc_grad_stats_scratch_bytes", "dfc_grad_stats", "dfc_clip_coef",
     "dfc_fiber_read", "dfc_fiber_write", "dfc_grad_stats_noalloc",
+    "dfc_zero_fused_step", "dfc_peer_barrier",
 )
 
 
@@ -94,6 +98,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_fiber_read": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_fiber_write": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
+        "dfc_zero_fused_step": ([P, P, I32, I32, P, I32, P, I32, I32, P, P], ctypes.c_int),
+        "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(h, name)

@@ -1,0 +1,299 @@
+// ZeRO-1 shard step fused with its collectives over NVLink peer memory.
+//
+// With the FP32 parameter vector and the bf16 compressed gradients in
+// symmetric (peer-mapped) memory on every rank, one kernel does what NCCL
+// reduce-scatter + dfc_mt_step + NCCL all-gather do, for this rank's pieces:
+//
+//   g      = (sum over ranks q = 0..N-1, in that order, of comp_q[j]) in FP32
+//   p, m, v = DFC-AdamW step (same element arithmetic as dfc_mt_step)
+//   param_q[j] = p  for every rank q (plain 128-bit stores to peer memory)
+//
+// Gradients cross NVLink once (2 B per element per peer) and parameters
+// once (4 B per element per peer), the reduction happens in registers in
+// FP32 (deterministic order, no bf16 re-rounding of partial sums), and no
+// reduce-scatter output buffer or all-gather staging is written to HBM.  Only
+// plain loads and stores touch peer memory (no TMA, no multicast).
+//
+// dfc_peer_barrier orders the ranks around it: each rank writes an epoch to
+// its slot in every peer's signal array (release, system scope) and then
+// waits for every peer's slot in its own array (acquire, system scope), for at
+// most a time limit; a rank that gives up sets an error flag and returns.
+#include <algorithm>
+#include <vector>
+
+#include "dfc_common.cuh"
+#include "dfc_step_elem.cuh"
+
+namespace dfc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kVec = 8;                      // elements per thread per tile
+constexpr int kTile = kThreads * kVec;       // 2048 elements per CTA
+constexpr int kMaxPeers = DFC_MAX_PEERS;
+
+struct PeerSegArg {
+  int64_t offset;  // flat element index of the segment's first element
+  int64_t n;
+  uint32_t* m;
+  uint32_t* v;
+  int32_t hyper;
+  int32_t vec;     // offset and n allow the 8-wide path
+};
+
+template <int MAXS, int MAXH>
+struct ZeroBatch {
+  const uint16_t* comp[kMaxPeers];  // every rank's compressed gradients (bf16 bits)
+  float* param[kMaxPeers];          // every rank's flat FP32 parameters
+  const float* dev_scale;
+  int32_t n_peers;
+  int32_t rank;
+  int32_t n_segs;
+  int32_t tile_base[MAXS + 1];
+  DfcHyper hyper[MAXH];
+  PeerSegArg seg[MAXS];
+};
+
+constexpr int kMaxSegs = 512, kMaxHypers = 16;
+static_assert(sizeof(ZeroBatch<kMaxSegs, kMaxHypers>) <= 32000, "launch parameter limit");
+
+__device__ __forceinline__ void bf16x8_add(float (&acc)[8], const uint4& c) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    acc[2 * k] = __fadd_rn(acc[2 * k], u2f(w[k] << 16));
+    acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], u2f(w[k] & 0xFFFF0000u));
+  }
+}
+
+template <int MODE, int MAXS, int MAXH>
+__device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
+                                     int64_t local, const Scalars& s) {
+  const int64_t j = sg.offset + local;
+  // g = comp_0[j], then + comp_q[j] for q = 1..N-1 (rank order)
+  float g[8];
+  const uint4 c0 = __ldcs(reinterpret_cast<const uint4*>(b.comp[0] + j));
+  const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    g[2 * k] = u2f(w0[k] << 16);
+    g[2 * k + 1] = u2f(w0[k] & 0xFFFF0000u);
+  }
+  for (int q = 1; q < b.n_peers; ++q)
+    bf16x8_add(g, __ldcs(reinterpret_cast<const uint4*>(b.comp[q] + j)));
+  float* mine = b.param[b.rank] + j;
+  float4 p0 = __ldcs(reinterpret_cast<const float4*>(mine));
+  float4 p1 = __ldcs(reinterpret_cast<const float4*>(mine + 4));
+  uint4 m0 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local));
+  uint4 m1 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local + 4));
+  uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local));
+  uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local + 4));
+  step_elem<MODE>(s, p0.x, g[0], m0.x, v0.x);
+  step_elem<MODE>(s, p0.y, g[1], m0.y, v0.y);
+  step_elem<MODE>(s, p0.z, g[2], m0.z, v0.z);
+  step_elem<MODE>(s, p0.w, g[3], m0.w, v0.w);
+  step_elem<MODE>(s, p1.x, g[4], m1.x, v1.x);
+  step_elem<MODE>(s, p1.y, g[5], m1.y, v1.y);
+  step_elem<MODE>(s, p1.z, g[6], m1.z, v1.z);
+  step_elem<MODE>(s, p1.w, g[7], m1.w, v1.w);
+  __stcs(reinterpret_cast<uint4*>(sg.m + local), m0);
+  __stcs(reinterpret_cast<uint4*>(sg.m + local + 4), m1);
+  __stcs(reinterpret_cast<uint4*>(sg.v + local), v0);
+  __stcs(reinterpret_cast<uint4*>(sg.v + local + 4), v1);
+  for (int q = 0; q < b.n_peers; ++q) {
+    float* dst = b.param[q] + j;
+    __stcs(reinterpret_cast<float4*>(dst), p0);
+    __stcs(reinterpret_cast<float4*>(dst + 4), p1);
+  }
+}
+
+template <int MODE, int MAXS, int MAXH>
+__device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
+                                        int64_t local, const Scalars& s) {
+  const int64_t j = sg.offset + local;
+  float g = bf16_bits_to_f32(b.comp[0][j]);
+  for (int q = 1; q < b.n_peers; ++q) g = __fadd_rn(g, bf16_bits_to_f32(b.comp[q][j]));
+  float p = b.param[b.rank][j];
+  uint32_t m = sg.m[local], v = sg.v[local];
+  step_elem<MODE>(s, p, g, m, v);
+  sg.m[local] = m;
+  sg.v[local] = v;
+  for (int q = 0; q < b.n_peers; ++q) b.param[q][j] = p;
+}
+
+template <int MODE, int MAXS, int MAXH>
+__global__ void __launch_bounds__(kThreads)
+    zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
+  const int32_t t = static_cast<int32_t>(blockIdx.x);
+  int lo = 0, hi = b.n_segs;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
+  }
+  const PeerSegArg& sg = b.seg[lo];
+  const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
+  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+  const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
+  int64_t done = 0;
+  if (sg.vec) {
+    const int64_t nv = count / kVec;
+    for (int64_t k = threadIdx.x; k < nv; k += kThreads) vec8<MODE>(b, sg, base + k * kVec, s);
+    done = nv * kVec;
+  }
+  for (int64_t k = done + threadIdx.x; k < count; k += kThreads) scalar1<MODE>(b, sg, base + k, s);
+}
+
+template <int MAXS, int MAXH>
+int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
+  const int32_t tiles = b.tile_base[b.n_segs];
+  if (tiles == 0) return DFC_OK;
+  switch (mode) {
+    case DFC_MODE_PLAIN: zero_step_kernel<DFC_MODE_PLAIN><<<tiles, kThreads, 0, st>>>(b); break;
+    case DFC_MODE_SIGNFIBER: zero_step_kernel<DFC_MODE_SIGNFIBER><<<tiles, kThreads, 0, st>>>(b); break;
+    default: zero_step_kernel<DFC_MODE_PACKED><<<tiles, kThreads, 0, st>>>(b); break;
+  }
+  return launch_status();
+}
+
+// ---- barrier --------------------------------------------------------------
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct BarrierArgs {
+  uint32_t* slots[kMaxPeers];  // every rank's signal array (n_peers words each)
+  int32_t n_peers;
+  int32_t rank;
+  uint32_t epoch;
+  int32_t* error;              // set to 1 + the peer waited for when the wait gives up
+  uint64_t timeout_ns;
+};
+
+__global__ void peer_barrier_kernel(const __grid_constant__ BarrierArgs a) {
+  const int q = threadIdx.x;
+  if (q >= a.n_peers) return;
+  __threadfence_system();  // this rank's earlier writes, local and remote, come first
+  st_release_sys(a.slots[q] + a.rank, a.epoch);
+  const uint32_t* mine = a.slots[a.rank] + q;
+  const uint64_t start = globaltimer();
+  while (static_cast<int32_t>(ld_acquire_sys(mine) - a.epoch) < 0) {
+    if (globaltimer() - start > a.timeout_ns) {
+      atomicExch(a.error, 1 + q);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+bool peers_ok(const void* const* ptrs, int32_t n) {
+  for (int32_t q = 0; q < n; ++q)
+    if (!ptrs[q]) return false;
+  return true;
+}
+
+}  // namespace
+}  // namespace dfc
+
+extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
+                                   int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
+                                   int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
+                                   int32_t mode, const float* device_grad_scale, void* stream) {
+  using namespace dfc;
+  if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers) return DFC_ERR_SIZE;
+  if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
+  if (mode != DFC_MODE_PLAIN && mode != DFC_MODE_SIGNFIBER && mode != DFC_MODE_PACKED)
+    return DFC_ERR_MODE;
+  if (n_segments == 0) return DFC_OK;
+  if (!comp_ptrs || !param_ptrs || !segments || (!hypers && n_hypers > 0)) return DFC_ERR_NULL;
+  if (!peers_ok(comp_ptrs, n_peers) || !peers_ok(param_ptrs, n_peers)) return DFC_ERR_NULL;
+  for (int32_t q = 0; q < n_peers; ++q)
+    if (!aligned(comp_ptrs[q], 16) || !aligned(param_ptrs[q], 16)) return DFC_ERR_ALIGN;
+  for (int32_t i = 0; i < n_segments; ++i) {
+    const DfcPeerSegment& s = segments[i];
+    if (s.numel < 0 || s.offset < 0) return DFC_ERR_SIZE;
+    if (s.numel == 0) continue;
+    if (!s.exp_avg || !s.exp_avg_sq) return DFC_ERR_NULL;
+    if (!aligned(s.exp_avg, 4) || !aligned(s.exp_avg_sq, 4)) return DFC_ERR_ALIGN;
+    if (s.hyper < 0 || s.hyper >= n_hypers) return DFC_ERR_HYPER;
+    if ((s.numel + kTile - 1) / kTile > INT32_MAX / 2) return DFC_ERR_SIZE;
+  }
+  ZeroBatch<kMaxSegs, kMaxHypers> b;
+  for (int32_t q = 0; q < kMaxPeers; ++q) {
+    b.comp[q] = q < n_peers ? static_cast<const uint16_t*>(comp_ptrs[q]) : nullptr;
+    b.param[q] = q < n_peers ? static_cast<float*>(param_ptrs[q]) : nullptr;
+  }
+  b.dev_scale = device_grad_scale;
+  b.n_peers = n_peers;
+  b.rank = rank;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<int32_t> local(static_cast<size_t>(n_hypers), -1);
+  std::vector<int32_t> used;
+  auto reset = [&]() {
+    for (int32_t g : used) local[g] = -1;
+    used.clear();
+    b.n_segs = 0;
+    b.tile_base[0] = 0;
+  };
+  reset();
+  for (int32_t i = 0; i < n_segments; ++i) {
+    const DfcPeerSegment& s = segments[i];
+    if (s.numel == 0) continue;
+    const int32_t tiles = static_cast<int32_t>((s.numel + kTile - 1) / kTile);
+    const bool need = local[s.hyper] < 0;
+    if (b.n_segs == kMaxSegs || (need && static_cast<int>(used.size()) == kMaxHypers) ||
+        b.tile_base[b.n_segs] > INT32_MAX - tiles) {
+      const int rc = launch(b, mode, st);
+      if (rc != DFC_OK) return rc;
+      reset();
+    }
+    if (local[s.hyper] < 0) {
+      local[s.hyper] = static_cast<int32_t>(used.size());
+      b.hyper[used.size()] = hypers[s.hyper];
+      used.push_back(s.hyper);
+    }
+    PeerSegArg& a = b.seg[b.n_segs];
+    a.offset = s.offset;
+    a.n = s.numel;
+    a.m = s.exp_avg;
+    a.v = s.exp_avg_sq;
+    a.hyper = local[s.hyper];
+    a.vec = (s.offset % 8 == 0) && aligned(s.exp_avg, 16) && aligned(s.exp_avg_sq, 16);
+    b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
+    ++b.n_segs;
+  }
+  return b.n_segs ? launch(b, mode, st) : DFC_OK;
+}
+
+extern "C" int dfc_peer_barrier(uint32_t* const* slot_ptrs, int32_t n_peers, int32_t rank,
+                                uint32_t epoch, int32_t* error_flag, int64_t timeout_ns,
+                                void* stream) {
+  using namespace dfc;
+  if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers || timeout_ns <= 0)
+    return DFC_ERR_SIZE;
+  if (!slot_ptrs || !error_flag || !peers_ok(reinterpret_cast<const void* const*>(slot_ptrs), n_peers))
+    return DFC_ERR_NULL;
+  for (int32_t q = 0; q < n_peers; ++q)
+    if (!aligned(slot_ptrs[q], 4)) return DFC_ERR_ALIGN;
+  if (!aligned(error_flag, 4)) return DFC_ERR_ALIGN;
+  BarrierArgs a;
+  for (int32_t q = 0; q < kMaxPeers; ++q) a.slots[q] = q < n_peers ? slot_ptrs[q] : nullptr;
+  a.n_peers = n_peers;
+  a.rank = rank;
+  a.epoch = epoch;
+  a.error = error_flag;
+  a.timeout_ns = static_cast<uint64_t>(timeout_ns);
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}

@@ -76,6 +76,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     reduce-scatter (default: on when the group has > 1 rank)
     average_grads   divide the summed gradient by the group size (default on)
     bucket_elems    elements per pipelined bucket (rounded to N*64)
+    transport       "nccl": NCCL reduce-scatter + step + NCCL all-gather;
+                    "peer": one fused kernel over NVLink peer memory
+                    (dfc_zero_fused_step) between two cross-GPU barriers;
+                    needs symmetric memory and compressed gradients
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -83,7 +87,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  weight_decay: float = 0.0, enable_fiber: bool = True, *,
                  moment_format: str = "packed", process_group=None,
                  compress_grads: bool | None = None, average_grads: bool = True,
-                 bucket_elems: int = DEFAULT_BUCKET, backend=None):
+                 bucket_elems: int = DEFAULT_BUCKET, transport: str = "nccl",
+                 barrier_timeout_s: float = 30.0, backend=None):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -99,7 +104,15 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.compress = (self.world > 1) if compress_grads is None else bool(compress_grads)
         self.average = bool(average_grads)
         self.kernels = backend if backend is not None else CudaKernels()
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport must be 'nccl' or 'peer'")
+        self.transport = transport if self.world > 1 else "nccl"
+        if self.transport == "peer" and not self.compress:
+            raise ValueError("the peer transport reduces bf16 compressed gradients")
+        self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
         self._layout(bucket_elems)
+        if self.transport == "peer":
+            self._setup_peer()
 
     # ---- layout -----------------------------------------------------------
     @torch.no_grad()
@@ -128,7 +141,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.n_buckets = -(-total // bucket)
         self.padded = self.n_buckets * bucket
         self.offsets = offs
-        self.flat_param = torch.zeros(self.padded, dtype=torch.float32, device=dev)
+        self.flat_param = self._alloc(self.padded, torch.float32)
         self.flat_grad = torch.zeros(self.padded, dtype=torch.float32, device=dev)
         for p, off in zip(self.params, offs):
             k = p.numel()
@@ -137,7 +150,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             p.grad = self.flat_grad[off:off + k].view_as(p)
         local = self.n_buckets * self.piece
         if self.compress:
-            self.comp = torch.zeros(self.padded, dtype=torch.int16, device=dev)
+            self.comp = self._alloc(self.padded, torch.int16)
             self.resid = torch.zeros(self.padded, dtype=torch.int16, device=dev)
             self.shard_grad = torch.zeros(local, dtype=torch.bfloat16, device=dev)
         elif n > 1:
@@ -166,6 +179,79 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             self.bucket_params.append(pidx)
         for p in self.params:
             self.state[p]["step"] = 0
+
+    def _alloc(self, n: int, dtype) -> torch.Tensor:
+        """Zeroed buffer; in symmetric (peer-mapped) memory for the peer transport."""
+        if self.transport == "peer":
+            import torch.distributed._symmetric_memory as symm_mem
+
+            t = symm_mem.empty(n, dtype=dtype, device=self.device)
+            return t.zero_()
+        return torch.zeros(n, dtype=dtype, device=self.device)
+
+    @torch.no_grad()
+    def _setup_peer(self):
+        """Exchange the peer addresses of the parameters, compressed
+        gradients and barrier slots (collective), and lay out this rank's
+        pieces as fused-kernel segments."""
+        import numpy as np
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group = self.group if self.group is not None else dist.group.WORLD
+        n = self.world
+
+        def peers(t):
+            h = symm_mem.rendezvous(t, group)
+            ptrs = [int(p) for p in h.buffer_ptrs]
+            off = t.data_ptr() - ptrs[self.rank]
+            nbytes = t.numel() * t.element_size()
+            # the tensor must lie inside this rank's buffer at the handle's
+            # offset, so the same offset addresses every peer's copy
+            if len(ptrs) != n or off < 0 or off + nbytes > int(h.buffer_size) or \
+                    (hasattr(h, "offset") and int(h.offset) != off):
+                raise RuntimeError("symmetric-memory layout is not the expected one")
+            return [p + off for p in ptrs], h
+
+        self.slots = symm_mem.empty(n, dtype=torch.int32, device=self.device).zero_()
+        self._param_peers, self._h_param = peers(self.flat_param)
+        self._comp_peers, self._h_comp = peers(self.comp)
+        self._slot_peers, self._h_slots = peers(self.slots)
+        self.peer_error = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._epoch = 0
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._comp_arr = np.array(self._comp_peers, dtype=np.uint64)
+        self._param_arr = np.array(self._param_peers, dtype=np.uint64)
+        self._slot_arr = np.array(self._slot_peers, dtype=np.uint64)
+        segs = []
+        for b, group_segs in enumerate(self.bucket_segments):
+            for (p, _, m, v), pi in zip(group_segs, self.bucket_params[b]):
+                off = (p.data_ptr() - self.flat_param.data_ptr()) // 4
+                segs.append((off, p.numel(), m.data_ptr(), v.data_ptr(), 0, 0))
+        self._peer_segs = np.array(segs, dtype=_lib.PEERSEG_DTYPE)
+        self._peer_seg_param = [pi for pidx in self.bucket_params for pi in pidx]
+
+    def _barrier(self, stream):
+        self._epoch += 1
+        _lib.check("dfc_peer_barrier", _lib.lib().dfc_peer_barrier(
+            _lib.ptr(self._slot_arr), self.world, self.rank, self._epoch & 0xFFFFFFFF,
+            self.peer_error.data_ptr(), self.barrier_timeout_ns, stream))
+
+    def _step_peer(self, rows, seg_hyper):
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.kernels.compress_ef(self.flat_grad, self.comp, self.resid)
+        self._barrier(stream)            # every rank's compressed gradients are complete
+        self._peer_segs["hyper"] = seg_hyper
+        with torch.cuda.device(self.device):
+            _lib.check("dfc_zero_fused_step", _lib.lib().dfc_zero_fused_step(
+                _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self.world, self.rank,
+                _lib.ptr(self._peer_segs), len(self._peer_segs),
+                _lib.ptr(kernels.hypers(rows)), len(rows), self.mode, None, stream))
+        self._barrier(stream)            # every rank's parameters are complete
+
+    def peer_status(self) -> int:
+        """0, or 1 + the rank a barrier gave up waiting for (synchronises)."""
+        return int(self.peer_error.item()) if self.transport == "peer" else 0
 
     def _bucket(self, t: torch.Tensor, b: int) -> torch.Tensor:
         return t[b * self.bucket:(b + 1) * self.bucket]
@@ -235,6 +321,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 idx.append(j)
             index.append(idx)
 
+        if self.transport == "peer":
+            self._step_peer(rows, [j for idx in index for j in idx])
+            return loss
+
         def reduce(b):
             if self.compress:
                 self.kernels.compress_ef(self._bucket(self.flat_grad, b),
@@ -281,6 +371,15 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     def full_reduced_grad(self) -> torch.Tensor:
         """The gradient the last step used, in flat order on every rank
         (collective; for checking and debugging)."""
+        if self.transport == "peer":
+            # the fused kernel sums every rank's bf16 values in FP32, rank order
+            allc = torch.empty(self.world * self.padded, dtype=torch.int16, device=self.device)
+            dist.all_gather_into_tensor(allc, self.comp, group=self.group)
+            parts = allc.view(self.world, self.padded).view(torch.bfloat16).float()
+            total = parts[0].clone()
+            for q in range(1, self.world):
+                total += parts[q]
+            return total
         out = torch.empty(self.padded, dtype=self.shard_grad.dtype, device=self.device)
         if self.world == 1:
             return out.copy_(self.shard_grad[:self.padded])

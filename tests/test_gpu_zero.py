@@ -23,7 +23,7 @@ def _grads(rank, step, sizes):
     return [(rng.standard_normal(n) * 1e-3).astype(np.float32) for n in sizes]
 
 
-def _run(rank, world, device, compress):
+def _run(rank, world, device, compress, transport="nccl"):
     from t3st_b200.zero import ShardedDFCAdamW
 
     torch.manual_seed(0)
@@ -31,7 +31,7 @@ def _run(rank, world, device, compress):
     sizes = [p.numel() for p in params]
     p0 = [p.detach().cpu().numpy().reshape(-1).copy() for p in params]
     opt = ShardedDFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed",
-                          compress_grads=compress, bucket_elems=8192)
+                          compress_grads=compress, bucket_elems=8192, transport=transport)
     sim_p = [x.copy() for x in p0]
     sim_m = [np.zeros(n, np.uint32) for n in sizes]
     sim_v = [np.zeros(n, np.uint32) for n in sizes]
@@ -44,8 +44,12 @@ def _run(rank, world, device, compress):
         opt.step()
         torch.cuda.synchronize()
         if world > 1:
-            red16 = opt.full_reduced_grad().view(torch.int16).cpu().numpy().view(np.uint16)
-            gsrc = [red16[off:off + n].copy() for off, n in zip(opt.offsets, sizes)]
+            red = opt.full_reduced_grad()
+            if red.dtype == torch.bfloat16:  # NCCL's bf16 sum
+                red = red.view(torch.int16).cpu().numpy().view(np.uint16)
+            else:                            # the fused kernel's FP32 sum, rank order
+                red = red.cpu().numpy()
+            gsrc = [red[off:off + n].copy() for off, n in zip(opt.offsets, sizes)]
             scale = 1.0 / world
         elif compress:
             flat = np.zeros(opt.padded, np.float32)
@@ -63,6 +67,7 @@ def _run(rank, world, device, compress):
         for i, p in enumerate(params):
             np.testing.assert_array_equal(p.detach().cpu().numpy().reshape(-1).view(np.uint32),
                                           sim_p[i].view(np.uint32))
+    assert opt.peer_status() == 0
     full = opt.consolidated_state_dict(to_rank=None)
     for i in range(len(sizes)):
         np.testing.assert_array_equal(full["state"][i]["exp_avg"].cpu().numpy().reshape(-1).view(np.uint32), sim_m[i])
@@ -92,7 +97,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, transport, q):
     try:
         import datetime
 
@@ -105,7 +110,7 @@ def _worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
-        _run(rank, world, dev, True)
+        _run(rank, world, dev, True, transport)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
@@ -113,7 +118,8 @@ def _worker(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
-def test_sharded_on_two_gpus_nccl():
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
+def test_sharded_on_two_gpus(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -121,7 +127,7 @@ def test_sharded_on_two_gpus_nccl():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
