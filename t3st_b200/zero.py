@@ -373,9 +373,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         (collective; for checking and debugging)."""
         if self.transport == "peer":
             # the fused kernel sums every rank's bf16 values in FP32, rank order
-            allc = torch.empty(self.world * self.padded, dtype=torch.int16, device=self.device)
-            dist.all_gather_into_tensor(allc, self.comp, group=self.group)
-            parts = allc.view(self.world, self.padded).view(torch.bfloat16).float()
+            allc = torch.empty(self.world * self.padded, dtype=torch.bfloat16, device=self.device)
+            dist.all_gather_into_tensor(allc, self.comp.view(torch.bfloat16), group=self.group)
+            parts = allc.view(self.world, self.padded).float()
             total = parts[0].clone()
             for q in range(1, self.world):
                 total += parts[q]
