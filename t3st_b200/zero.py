@@ -13,11 +13,17 @@ per bucket b, pipelined across buckets:
          grad_scale = 1/N to average), packed moment words by default;
   AG(b)  NCCL all-gather of the updated FP32 piece into every rank's bucket.
 
-The host issues C(0) RS(0), then for each b: C(b+1) RS(b+1), wait RS(b),
-S(b) AG(b).  The collectives run in that order on NCCL's stream and the
-kernels on the caller's stream, so the compression and step of one bucket
-overlap the transfers of its neighbours; the step returns with the caller's
-stream ordered after the last all-gather.
+With transport="nccl" the host issues C(0) RS(0), then for each b: C(b+1)
+RS(b+1), wait RS(b), S(b) AG(b); the collectives run in that order on
+NCCL's stream and the kernels on the caller's stream.  With transport="peer"
+(the fast path) RS, S and AG of a bucket are one kernel over NVLink peer
+memory (dfc_zero_fused_step): it reads every rank's bf16 values of its
+piece, sums them in FP32 in rank order, steps, and stores the new FP32
+parameters into every rank's copy; a cross-GPU barrier before it (every
+rank's C(b) done) and one at the end of the step (every rank's parameters
+done) order the ranks, and C(b+1) on the caller's stream overlaps the fused
+kernel of bucket b on a side stream.  Either way the step returns with the
+caller's stream ordered after all of it.
 
 The parameters are re-homed into one flat FP32 buffer (each becomes a view
 of it) and their ``.grad`` into one flat gradient buffer, so the collectives
@@ -223,13 +229,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self._comp_arr = np.array(self._comp_peers, dtype=np.uint64)
         self._param_arr = np.array(self._param_peers, dtype=np.uint64)
         self._slot_arr = np.array(self._slot_peers, dtype=np.uint64)
-        segs = []
-        for b, group_segs in enumerate(self.bucket_segments):
-            for (p, _, m, v), pi in zip(group_segs, self.bucket_params[b]):
-                off = (p.data_ptr() - self.flat_param.data_ptr()) // 4
-                segs.append((off, p.numel(), m.data_ptr(), v.data_ptr(), 0, 0))
-        self._peer_segs = np.array(segs, dtype=_lib.PEERSEG_DTYPE)
-        self._peer_seg_param = [pi for pidx in self.bucket_params for pi in pidx]
+        self._peer_segs = []
+        for group_segs in self.bucket_segments:
+            segs = [((p.data_ptr() - self.flat_param.data_ptr()) // 4, p.numel(), m.data_ptr(),
+                     v.data_ptr(), 0, 0) for p, _, m, v in group_segs]
+            self._peer_segs.append(np.array(segs, dtype=_lib.PEERSEG_DTYPE))
+        self._side = torch.cuda.Stream(self.device)
 
     def _barrier(self, stream):
         self._epoch += 1
@@ -237,17 +242,33 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             _lib.ptr(self._slot_arr), self.world, self.rank, self._epoch & 0xFFFFFFFF,
             self.peer_error.data_ptr(), self.barrier_timeout_ns, stream))
 
-    def _step_peer(self, rows, seg_hyper):
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        self.kernels.compress_ef(self.flat_grad, self.comp, self.resid)
-        self._barrier(stream)            # every rank's compressed gradients are complete
-        self._peer_segs["hyper"] = seg_hyper
+    def _step_peer(self, rows, index):
+        """Bucket b: compress on the caller's stream; then, on a side stream
+        that waits for it, a barrier (every rank's bucket-b gradients are
+        complete) and the fused step of bucket b -- which runs while the
+        caller's stream compresses bucket b+1.  A last barrier (every rank's
+        parameters are complete) ends the step; the caller's stream waits
+        for it."""
+        main = torch.cuda.current_stream(self.device)
+        side = self._side
+        hyp = kernels.hypers(rows)
+        lib = _lib.lib()
+        side.wait_stream(main)
         with torch.cuda.device(self.device):
-            _lib.check("dfc_zero_fused_step", _lib.lib().dfc_zero_fused_step(
-                _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self.world, self.rank,
-                _lib.ptr(self._peer_segs), len(self._peer_segs),
-                _lib.ptr(kernels.hypers(rows)), len(rows), self.mode, None, stream))
-        self._barrier(stream)            # every rank's parameters are complete
+            for b in range(self.n_buckets):
+                self.kernels.compress_ef(self._bucket(self.flat_grad, b), self._bucket(self.comp, b),
+                                         self._bucket(self.resid, b))
+                side.wait_stream(main)
+                self._barrier(side.cuda_stream)
+                segs = self._peer_segs[b]
+                if len(segs):
+                    segs["hyper"] = index[b]
+                    _lib.check("dfc_zero_fused_step", lib.dfc_zero_fused_step(
+                        _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self.world,
+                        self.rank, _lib.ptr(segs), len(segs), _lib.ptr(hyp), len(rows),
+                        self.mode, None, side.cuda_stream))
+            self._barrier(side.cuda_stream)
+        main.wait_stream(side)
 
     def peer_status(self) -> int:
         """0, or 1 + the rank a barrier gave up waiting for (synchronises)."""
@@ -322,7 +343,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             index.append(idx)
 
         if self.transport == "peer":
-            self._step_peer(rows, [j for idx in index for j in idx])
+            self._step_peer(rows, index)
             return loss
 
         def reduce(b):
