@@ -60,8 +60,9 @@ def parse_args():
                     help="skip the nvidia-smi clock sampler (profiling runs)")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
-    ap.add_argument("--transport", choices=("peer", "nccl"), default="peer",
-                    help="N>1: fused kernel over NVLink peer memory, or NCCL collectives")
+    ap.add_argument("--transport", choices=("auto", "peer", "nccl"), default="auto",
+                    help="N>1: fused kernel over NVLink peer memory, NCCL collectives, or "
+                         "the measured faster of the two for N (peer at 2 ranks)")
     return ap.parse_args()
 
 
@@ -520,7 +521,7 @@ def run_sharded(args, rank, world, device):
                             "memory between two barriers; nccl: reduce-scatter + step + "
                             "all-gather)",
                 "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
-                "transport": args.transport,
+                "transport": opt.transport,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
             },
             "roofline": {"bound": "nvlink" if t_nvl > t_hbm else "hbm",
@@ -529,7 +530,8 @@ def run_sharded(args, rank, world, device):
                          "hbm_bytes_per_rank": hbm_bytes, "nvlink_bytes_per_rank": nvl_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": f"{peak_kind} hbm_gbs",
                          "nvlink_gbs": NVLINK_GBS, "traffic": None},
-            "gpu_launches": K * (4 if args.transport == "peer" else 2 * opt.n_buckets),
+            "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport == "peer"
+                                 else 2 * opt.n_buckets),
             "clocks": clocks,
         }
     if not args.no_e2e:

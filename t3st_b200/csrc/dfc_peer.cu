@@ -66,21 +66,19 @@ __device__ __forceinline__ void bf16x8_add(float (&acc)[8], const uint4& c) {
   }
 }
 
-template <int MODE, int MAXS, int MAXH>
+// NP = number of ranks when known at compile time (2, 4, 8), 0 = any (up to
+// kMaxPeers, predicated).  All peer loads are issued before the first add so
+// the remote latencies overlap instead of adding up.
+template <int MODE, int NP, int MAXS, int MAXH>
 __device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
                                      int64_t local, const Scalars& s) {
+  constexpr int kLoads = NP ? NP : kMaxPeers;
+  const int np = NP ? NP : b.n_peers;
   const int64_t j = sg.offset + local;
-  // g = comp_0[j], then + comp_q[j] for q = 1..N-1 (rank order)
-  float g[8];
-  const uint4 c0 = __ldcs(reinterpret_cast<const uint4*>(b.comp[0] + j));
-  const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+  uint4 c[kLoads];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    g[2 * k] = u2f(w0[k] << 16);
-    g[2 * k + 1] = u2f(w0[k] & 0xFFFF0000u);
-  }
-  for (int q = 1; q < b.n_peers; ++q)
-    bf16x8_add(g, __ldcs(reinterpret_cast<const uint4*>(b.comp[q] + j)));
+  for (int q = 0; q < kLoads; ++q)
+    if (NP || q < np) c[q] = __ldcs(reinterpret_cast<const uint4*>(b.comp[q] + j));
   float* mine = b.param[b.rank] + j;
   float4 p0 = __ldcs(reinterpret_cast<const float4*>(mine));
   float4 p1 = __ldcs(reinterpret_cast<const float4*>(mine + 4));
@@ -88,6 +86,17 @@ __device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerS
   uint4 m1 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local + 4));
   uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local));
   uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local + 4));
+  // g = comp_0[j], then + comp_q[j] for q = 1..N-1 (rank order)
+  float g[8];
+  const uint32_t w0[4] = {c[0].x, c[0].y, c[0].z, c[0].w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    g[2 * k] = u2f(w0[k] << 16);
+    g[2 * k + 1] = u2f(w0[k] & 0xFFFF0000u);
+  }
+#pragma unroll
+  for (int q = 1; q < kLoads; ++q)
+    if (NP || q < np) bf16x8_add(g, c[q]);
   step_elem<MODE>(s, p0.x, g[0], m0.x, v0.x);
   step_elem<MODE>(s, p0.y, g[1], m0.y, v0.y);
   step_elem<MODE>(s, p0.z, g[2], m0.z, v0.z);
@@ -100,10 +109,13 @@ __device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerS
   __stcs(reinterpret_cast<uint4*>(sg.m + local + 4), m1);
   __stcs(reinterpret_cast<uint4*>(sg.v + local), v0);
   __stcs(reinterpret_cast<uint4*>(sg.v + local + 4), v1);
-  for (int q = 0; q < b.n_peers; ++q) {
-    float* dst = b.param[q] + j;
-    __stcs(reinterpret_cast<float4*>(dst), p0);
-    __stcs(reinterpret_cast<float4*>(dst + 4), p1);
+#pragma unroll
+  for (int q = 0; q < kLoads; ++q) {
+    if (NP || q < np) {
+      float* dst = b.param[q] + j;
+      __stcs(reinterpret_cast<float4*>(dst), p0);
+      __stcs(reinterpret_cast<float4*>(dst + 4), p1);
+    }
   }
 }
 
@@ -121,7 +133,7 @@ __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const Pe
   for (int q = 0; q < b.n_peers; ++q) b.param[q][j] = p;
 }
 
-template <int MODE, int MAXS, int MAXH>
+template <int MODE, int NP, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
   const int32_t t = static_cast<int32_t>(blockIdx.x);
@@ -137,10 +149,20 @@ __global__ void __launch_bounds__(kThreads)
   int64_t done = 0;
   if (sg.vec) {
     const int64_t nv = count / kVec;
-    for (int64_t k = threadIdx.x; k < nv; k += kThreads) vec8<MODE>(b, sg, base + k * kVec, s);
+    for (int64_t k = threadIdx.x; k < nv; k += kThreads) vec8<MODE, NP>(b, sg, base + k * kVec, s);
     done = nv * kVec;
   }
   for (int64_t k = done + threadIdx.x; k < count; k += kThreads) scalar1<MODE>(b, sg, base + k, s);
+}
+
+template <int MODE, int MAXS, int MAXH>
+void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t tiles, cudaStream_t st) {
+  switch (b.n_peers) {
+    case 2: zero_step_kernel<MODE, 2><<<tiles, kThreads, 0, st>>>(b); break;
+    case 4: zero_step_kernel<MODE, 4><<<tiles, kThreads, 0, st>>>(b); break;
+    case 8: zero_step_kernel<MODE, 8><<<tiles, kThreads, 0, st>>>(b); break;
+    default: zero_step_kernel<MODE, 0><<<tiles, kThreads, 0, st>>>(b); break;
+  }
 }
 
 template <int MAXS, int MAXH>
@@ -148,9 +170,9 @@ int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
   const int32_t tiles = b.tile_base[b.n_segs];
   if (tiles == 0) return DFC_OK;
   switch (mode) {
-    case DFC_MODE_PLAIN: zero_step_kernel<DFC_MODE_PLAIN><<<tiles, kThreads, 0, st>>>(b); break;
-    case DFC_MODE_SIGNFIBER: zero_step_kernel<DFC_MODE_SIGNFIBER><<<tiles, kThreads, 0, st>>>(b); break;
-    default: zero_step_kernel<DFC_MODE_PACKED><<<tiles, kThreads, 0, st>>>(b); break;
+    case DFC_MODE_PLAIN: launch_np<DFC_MODE_PLAIN>(b, tiles, st); break;
+    case DFC_MODE_SIGNFIBER: launch_np<DFC_MODE_SIGNFIBER>(b, tiles, st); break;
+    default: launch_np<DFC_MODE_PACKED>(b, tiles, st); break;
   }
   return launch_status();
 }

@@ -85,7 +85,13 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     transport       "nccl": NCCL reduce-scatter + step + NCCL all-gather;
                     "peer": one fused kernel over NVLink peer memory
                     (dfc_zero_fused_step) between two cross-GPU barriers;
-                    needs symmetric memory and compressed gradients
+                    needs symmetric memory and compressed gradients;
+                    "auto" (default): "peer" for 2 ranks, "nccl" for more --
+                    measured on B200 over a 2^30-element vector: 2 ranks
+                    7.6 ms (peer) vs 10.5 ms (nccl); 4 ranks 13.7 vs 11.1;
+                    8 ranks 16.3 vs 11.3 (the fused kernel sends every
+                    parameter to each peer with plain stores, NCCL does
+                    better once there are more than two ranks)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -93,7 +99,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  weight_decay: float = 0.0, enable_fiber: bool = True, *,
                  moment_format: str = "packed", process_group=None,
                  compress_grads: bool | None = None, average_grads: bool = True,
-                 bucket_elems: int = DEFAULT_BUCKET, transport: str = "nccl",
+                 bucket_elems: int = DEFAULT_BUCKET, transport: str = "auto",
                  barrier_timeout_s: float = 30.0, backend=None):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
@@ -110,8 +116,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.compress = (self.world > 1) if compress_grads is None else bool(compress_grads)
         self.average = bool(average_grads)
         self.kernels = backend if backend is not None else CudaKernels()
-        if transport not in ("nccl", "peer"):
-            raise ValueError("transport must be 'nccl' or 'peer'")
+        if transport not in ("auto", "nccl", "peer"):
+            raise ValueError("transport must be 'auto', 'nccl' or 'peer'")
+        if transport == "auto":
+            on_cuda = all(p.is_cuda for g in self.param_groups for p in g["params"])
+            fused_ok = self.world == 2 and self.compress and backend is None and on_cuda
+            transport = "peer" if fused_ok else "nccl"
         self.transport = transport if self.world > 1 else "nccl"
         if self.transport == "peer" and not self.compress:
             raise ValueError("the peer transport reduces bf16 compressed gradients")
