@@ -67,20 +67,28 @@ extern "C" {
  * stores FP32 moments). */
 #define DFC_MODE_PACKED 2
 
-/* ---- gradient element types ---- */
-#define DFC_GRAD_F32 0
-#define DFC_GRAD_BF16 1
+/* ---- element types of parameters and gradients ---- */
+#define DFC_DTYPE_F32 0
+#define DFC_DTYPE_BF16 1
+#define DFC_DTYPE_F16 2
+#define DFC_GRAD_F32 DFC_DTYPE_F32
+#define DFC_GRAD_BF16 DFC_DTYPE_BF16
+#define DFC_GRAD_F16 DFC_DTYPE_F16
 
 /* One contiguous run of elements updated by the step: a whole parameter, or
- * the part of one that falls in a shard.  48 bytes. */
+ * the part of one that falls in a shard.  bf16/fp16 parameters keep FP32
+ * moments; their update is computed in FP32 and rounded once to the
+ * parameter type, with m and den rounded to it first, as PyTorch does for
+ * the reference's mul_/addcdiv_ (remote/torch_fiber.py:114-116).  48 bytes. */
 typedef struct DfcSegment {
-  float* param;          /* FP32, updated in place */
-  const void* grad;      /* DFC_GRAD_F32 (float) or DFC_GRAD_BF16 (bf16 bits) */
+  void* param;           /* param_dtype elements, updated in place */
+  const void* grad;      /* grad_dtype elements */
   uint32_t* exp_avg;     /* first-moment words, updated in place */
   uint32_t* exp_avg_sq;  /* second-moment words, updated in place */
   int64_t numel;
   int32_t hyper;         /* index into the call's DfcHyper array */
-  int32_t grad_dtype;    /* DFC_GRAD_* */
+  int16_t grad_dtype;    /* DFC_DTYPE_* */
+  int16_t param_dtype;   /* DFC_DTYPE_* */
 } DfcSegment;
 
 /* FP32 scalars of one (param group, step count) pair, each rounded once

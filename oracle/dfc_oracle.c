@@ -20,6 +20,14 @@
  * strips bit 31 of the second-moment word before the update and puts it back
  * afterwards (torch_fiber.py:18-19, 90-107).
  *
+ * Reduced-precision parameters (bf16/fp16, remote/torch_fiber.py:45, 114-116):
+ * the moments stay FP32; PyTorch's CPU kernels compute mul_ and addcdiv_ in
+ * FP32 and round once to the parameter type, with m and den rounded to it
+ * first (first.to(parameter.dtype), denominator.to(parameter.dtype)):
+ *   p1 = lo(p * decay);  p' = lo(p1 + (f32(-lr/bc1) * lo(m')) / lo(den))
+ * lo() rounds to nearest even; a NaN becomes the canonical quiet NaN of the
+ * type (bf16 0x7FC0, fp16 0x7E00).
+ *
  * Two formats have no counterpart in the reference and are specified here:
  *
  * Packed moment word (bf16 high half + 16-bit error-feedback residual low
@@ -47,6 +55,11 @@
 #define ORC_MODE_PLAIN 0
 #define ORC_MODE_SIGNFIBER 1
 #define ORC_MODE_PACKED 2
+
+/* element types of parameters and gradients */
+#define ORC_F32 0
+#define ORC_BF16 1
+#define ORC_F16 2
 
 typedef struct orc_hyper {
   float beta1;
@@ -101,9 +114,50 @@ float orc_unpack_signed(uint32_t w) {
 
 static inline float bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
 
+/* round to nearest even, NaN -> 0x7FC0 */
+static inline uint16_t f32_to_bf16(float x) {
+  uint32_t b = f2u(x);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0u;
+  return (uint16_t)((b + 0x7FFFu + ((b >> 16) & 1u)) >> 16);
+}
+
+static inline float f16_to_f32(uint16_t h) {
+  _Float16 v;
+  memcpy(&v, &h, 2);
+  return (float)v;
+}
+
+/* round to nearest even (IEEE conversion), NaN -> 0x7E00 */
+static inline uint16_t f32_to_f16(float x) {
+  if (isnan(x)) return 0x7E00u;
+  _Float16 v = (_Float16)x;
+  uint16_t h;
+  memcpy(&h, &v, 2);
+  return h;
+}
+
+static inline float load_elem(int dt, const void* base, int64_t i) {
+  if (dt == ORC_BF16) return bf16_to_f32(((const uint16_t*)base)[i]);
+  if (dt == ORC_F16) return f16_to_f32(((const uint16_t*)base)[i]);
+  return ((const float*)base)[i];
+}
+
+static inline void store_elem(int dt, void* base, int64_t i, float x) {
+  if (dt == ORC_BF16) ((uint16_t*)base)[i] = f32_to_bf16(x);
+  else if (dt == ORC_F16) ((uint16_t*)base)[i] = f32_to_f16(x);
+  else ((float*)base)[i] = x;
+}
+
+/* value of x rounded to the parameter type */
+static inline float round_to(int dt, float x) {
+  if (dt == ORC_BF16) return bf16_to_f32(f32_to_bf16(x));
+  if (dt == ORC_F16) return f16_to_f32(f32_to_f16(x));
+  return x;
+}
+
 /* ---- one element of the step ---- */
-static inline void step_one(int mode, const orc_hyper* h, float* p, float gin, uint32_t* mw,
-                            uint32_t* vw) {
+static inline void step_one(int mode, int pdt, const orc_hyper* h, float* p, float gin,
+                            uint32_t* mw, uint32_t* vw) {
   float g = gin * h->grad_scale;
   float m, v;
   uint32_t payload = 0;
@@ -136,24 +190,28 @@ static inline void step_one(int mode, const orc_hyper* h, float* p, float gin, u
     v_store = payload | (mode == ORC_MODE_PACKED ? orc_enc_mag(mag) : mag);
   }
   float den = sqrtf(v_upd) / h->sqrt_bc2 + h->eps;
-  float p1 = *p * h->decay;
-  float upd = (h->neg_step_size * m_new) / den;
-  *p = p1 + upd;
+  if (pdt == ORC_F32) {
+    float p1 = *p * h->decay;
+    float upd = (h->neg_step_size * m_new) / den;
+    *p = p1 + upd;
+  } else {
+    float p1 = round_to(pdt, *p * h->decay);
+    float upd = (h->neg_step_size * round_to(pdt, m_new)) / round_to(pdt, den);
+    *p = round_to(pdt, p1 + upd);
+  }
   *mw = (mode == ORC_MODE_PACKED) ? orc_pack_signed(m_new) : f2u(m_new);
   *vw = v_store;
 }
 
-int orc_step_f32(int mode, const orc_hyper* h, float* p, const float* g, uint32_t* m, uint32_t* v,
-                 int64_t n) {
-  if (mode < 0 || mode > 2) return -1;
-  for (int64_t i = 0; i < n; ++i) step_one(mode, h, p + i, g[i], m + i, v + i);
-  return 0;
-}
-
-int orc_step_bf16(int mode, const orc_hyper* h, float* p, const uint16_t* g, uint32_t* m,
-                  uint32_t* v, int64_t n) {
-  if (mode < 0 || mode > 2) return -1;
-  for (int64_t i = 0; i < n; ++i) step_one(mode, h, p + i, bf16_to_f32(g[i]), m + i, v + i);
+/* p: parameters of type pdt, g: gradients of type gdt (ORC_F32/BF16/F16) */
+int orc_step(int mode, const orc_hyper* h, void* p, int pdt, const void* g, int gdt, uint32_t* m,
+             uint32_t* v, int64_t n) {
+  if (mode < 0 || mode > 2 || pdt < 0 || pdt > 2 || gdt < 0 || gdt > 2) return -1;
+  for (int64_t i = 0; i < n; ++i) {
+    float pv = load_elem(pdt, p, i);
+    step_one(mode, pdt, h, &pv, load_elem(gdt, g, i), m + i, v + i);
+    store_elem(pdt, p, i, pv);
+  }
   return 0;
 }
 

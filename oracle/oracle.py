@@ -35,6 +35,9 @@ MODE_PLAIN = 0
 MODE_SIGNFIBER = 1
 MODE_PACKED = 2
 
+F32, BF16, F16 = 0, 1, 2
+DTYPES = {"f32": F32, "bf16": BF16, "f16": F16}
+
 CFLAGS = ["-O2", "-fPIC", "-shared", "-std=c11", "-ffp-contract=off", "-fno-fast-math",
           "-fexcess-precision=standard"]
 
@@ -63,8 +66,8 @@ def lib():
         handle = ctypes.CDLL(build())
         P = ctypes.c_void_p
         I64 = ctypes.c_int64
-        handle.orc_step_f32.argtypes = [ctypes.c_int, ctypes.POINTER(_Hyper), P, P, P, P, I64]
-        handle.orc_step_bf16.argtypes = [ctypes.c_int, ctypes.POINTER(_Hyper), P, P, P, P, I64]
+        handle.orc_step.argtypes = [ctypes.c_int, ctypes.POINTER(_Hyper), P, ctypes.c_int, P,
+                                    ctypes.c_int, P, P, I64]
         for name in ("orc_pack_first", "orc_unpack_first", "orc_pack_second", "orc_unpack_second"):
             getattr(handle, name).argtypes = [P, P, I64]
         handle.orc_compress_ef.argtypes = [P, P, P, I64]
@@ -130,19 +133,23 @@ def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
-def step(mode: int, hyper: Hyper, p: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray) -> None:
-    """In-place element-wise step.  p float32; g float32 or bf16 bits (uint16);
-    m, v uint32 words (FP32 bit patterns, or packed words in MODE_PACKED)."""
+def step(mode: int, hyper: Hyper, p: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray,
+         param_dtype: str = "bf16", grad_dtype: str = "bf16") -> None:
+    """In-place element-wise step.  p: float32, or uint16 bits of a
+    ``param_dtype`` ("bf16"/"f16") parameter; g: float32, or uint16 bits of a
+    ``grad_dtype`` gradient; m, v uint32 words (FP32 bit patterns, or packed
+    words in MODE_PACKED)."""
     n = p.size
-    assert p.dtype == np.float32 and m.dtype == np.uint32 and v.dtype == np.uint32
+    assert m.dtype == np.uint32 and v.dtype == np.uint32
     assert g.size == n and m.size == n and v.size == n
+    pdt = F32 if p.dtype == np.float32 else DTYPES[param_dtype]
+    gdt = F32 if g.dtype == np.float32 else DTYPES[grad_dtype]
+    if pdt != F32:
+        assert p.dtype == np.uint16
+    if gdt != F32:
+        assert g.dtype == np.uint16
     h = hyper.ctype()
-    if g.dtype == np.float32:
-        rc = lib().orc_step_f32(mode, ctypes.byref(h), _ptr(p), _ptr(g), _ptr(m), _ptr(v), n)
-    elif g.dtype == np.uint16:
-        rc = lib().orc_step_bf16(mode, ctypes.byref(h), _ptr(p), _ptr(g), _ptr(m), _ptr(v), n)
-    else:
-        raise TypeError(g.dtype)
+    rc = lib().orc_step(mode, ctypes.byref(h), _ptr(p), pdt, _ptr(g), gdt, _ptr(m), _ptr(v), n)
     if rc != 0:
         raise ValueError(f"oracle step failed: {rc}")
 
@@ -197,11 +204,13 @@ def grad_stats(g: np.ndarray) -> tuple[float, float, int]:
     return s.value, a.value, bad.value
 
 
-def multi_tensor_step(mode, tensors, grads, group, steps):
+def multi_tensor_step(mode, tensors, grads, group, steps, param_dtype="bf16"):
     """Reference bookkeeping over a parameter list (remote/torch_fiber.py:74-117).
 
-    tensors: list of dicts with 'p' (float32), 'm', 'v' (uint32 words), updated in place.
-    grads:   list of float32 arrays or None (None skips the tensor, step not advanced).
+    tensors: list of dicts with 'p' (float32, or uint16 bits of param_dtype), 'm', 'v'
+             (uint32 words), updated in place.
+    grads:   list of arrays of the parameter's type, or None (None skips the
+             tensor, step not advanced).
     group:   dict(lr, betas, eps, weight_decay[, grad_scale]).
     steps:   list[int] per-tensor step counters, advanced in place.
     """
@@ -211,7 +220,7 @@ def multi_tensor_step(mode, tensors, grads, group, steps):
         steps[i] += 1
         h = reference_hyper(group["lr"], group["betas"], group["eps"], group["weight_decay"],
                             steps[i], group.get("grad_scale", 1.0))
-        step(mode, h, t["p"], np.ascontiguousarray(g), t["m"], t["v"])
+        step(mode, h, t["p"], np.ascontiguousarray(g), t["m"], t["v"], param_dtype, param_dtype)
 
 
 def f32_ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:

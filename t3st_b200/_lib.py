@@ -36,13 +36,15 @@ MODE_PLAIN = 0
 MODE_SIGNFIBER = 1
 MODE_PACKED = 2
 
-GRAD_F32 = 0
-GRAD_BF16 = 1
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+DTYPE_F16 = 2
+GRAD_F32, GRAD_BF16, GRAD_F16 = DTYPE_F32, DTYPE_BF16, DTYPE_F16
 
 # numpy mirrors of the descriptor structs (same byte layout as the C structs)
 SEGMENT_DTYPE = np.dtype([("param", "<u8"), ("grad", "<u8"), ("exp_avg", "<u8"),
                           ("exp_avg_sq", "<u8"), ("numel", "<i8"), ("hyper", "<i4"),
-                          ("grad_dtype", "<i4")])
+                          ("grad_dtype", "<i2"), ("param_dtype", "<i2")])
 HYPER_FIELDS = ("beta1", "one_minus_beta1", "beta2", "one_minus_beta2", "sqrt_bc2", "eps",
                 "decay", "neg_step_size", "grad_scale")
 HYPER_DTYPE = np.dtype([(f, "<f4") for f in HYPER_FIELDS] + [("reserved", "<f4", (3,))])

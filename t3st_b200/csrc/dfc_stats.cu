@@ -12,6 +12,7 @@
 #include <math.h>
 
 #include "dfc_common.cuh"
+#include "dfc_step_elem.cuh"
 
 namespace dfc {
 namespace {
@@ -24,8 +25,8 @@ constexpr int kMaxBufs = 1000;
 struct BufArg {
   const void* g;
   int64_t n;
-  int32_t bf16;
-  int32_t vec;
+  int32_t dtype;  // DFC_DTYPE_*
+  int32_t vec;    // FP32 and 16-byte aligned
 };
 
 struct StatsBatch {
@@ -68,8 +69,9 @@ __device__ __forceinline__ Acc warp_fold(Acc acc) {
 }
 
 __device__ __forceinline__ float load1(const BufArg& b, int64_t i) {
-  return b.bf16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(b.g)[i])
-                : static_cast<const float*>(b.g)[i];
+  if (b.dtype == DFC_DTYPE_BF16) return from_bits16<DFC_DTYPE_BF16>(static_cast<const uint16_t*>(b.g)[i]);
+  if (b.dtype == DFC_DTYPE_F16) return from_bits16<DFC_DTYPE_F16>(static_cast<const uint16_t*>(b.g)[i]);
+  return static_cast<const float*>(b.g)[i];
 }
 
 __global__ void __launch_bounds__(kThreads) stats_partial_kernel(const __grid_constant__ StatsBatch b) {
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) stats_partial_kernel(const __grid_co
 
   Acc acc{0.0, 0.0f, 0};
   int64_t done = 0;
-  if (buf.vec && !buf.bf16) {
+  if (buf.vec) {
     const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(buf.g) + base);
     const int64_t nv = count / 4;
     for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
@@ -142,10 +144,12 @@ int64_t tiles_of(int64_t n) { return (n + kTile - 1) / kTile; }
 
 int validate(const DfcGradRef& r) {
   if (r.numel < 0) return DFC_ERR_SIZE;
-  if (r.grad_dtype != DFC_GRAD_F32 && r.grad_dtype != DFC_GRAD_BF16) return DFC_ERR_DTYPE;
+  if (r.grad_dtype != DFC_DTYPE_F32 && r.grad_dtype != DFC_DTYPE_BF16 &&
+      r.grad_dtype != DFC_DTYPE_F16)
+    return DFC_ERR_DTYPE;
   if (r.numel == 0) return DFC_OK;
   if (!r.grad) return DFC_ERR_NULL;
-  if (!aligned(r.grad, r.grad_dtype == DFC_GRAD_BF16 ? 2 : 4)) return DFC_ERR_ALIGN;
+  if (!aligned(r.grad, r.grad_dtype == DFC_DTYPE_F32 ? 4 : 2)) return DFC_ERR_ALIGN;
   if (tiles_of(r.numel) > INT32_MAX / 2) return DFC_ERR_SIZE;
   return DFC_OK;
 }
@@ -172,8 +176,8 @@ int grad_stats_launch(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* ou
       BufArg a;
       a.g = grads[i].grad;
       a.n = grads[i].numel;
-      a.bf16 = grads[i].grad_dtype == DFC_GRAD_BF16;
-      a.vec = aligned(grads[i].grad, 16);
+      a.dtype = grads[i].grad_dtype;
+      a.vec = grads[i].grad_dtype == DFC_DTYPE_F32 && aligned(grads[i].grad, 16);
       b.buf[b.n_bufs] = a;
       b.tile_base[b.n_bufs + 1] = b.tile_base[b.n_bufs] + static_cast<int32_t>(tl);
       ++b.n_bufs;

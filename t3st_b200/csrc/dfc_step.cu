@@ -44,11 +44,11 @@ constexpr int kVec = 4;
 constexpr int kUnroll = DFC_STEP_UNROLL;
 constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA
 
-constexpr int32_t kFlagBf16 = 1;
-constexpr int32_t kFlagVec = 2;
+// SegArg.flags: bit 0 = the four-element vector path is aligned.
+constexpr int32_t kFlagVec = 1;
 
 struct SegArg {
-  float* p;
+  void* p;
   const void* g;
   uint32_t* m;
   uint32_t* v;
@@ -71,54 +71,71 @@ constexpr int kSmallSegs = 64, kSmallHypers = 8;
 constexpr int kLargeSegs = 560, kLargeHypers = 32;
 static_assert(sizeof(StepBatch<kLargeSegs, kLargeHypers>) <= 32000, "launch parameter limit");
 
-template <bool BF16>
-__device__ __forceinline__ float4 load_grad4(const void* g, int64_t i) {
-  if (BF16) {
-    const uint2 b = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(g) + i));
-    return make_float4(u2f(b.x << 16), u2f(b.x & 0xFFFF0000u), u2f(b.y << 16),
-                       u2f(b.y & 0xFFFF0000u));
+// four consecutive elements of type DT at base[i] (i a multiple of 4)
+template <int DT>
+__device__ __forceinline__ float4 load4(const void* base, int64_t i) {
+  if (DT == DFC_DTYPE_F32)
+    return __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(base) + i));
+  const uint2 b = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + i));
+  return make_float4(from_bits16<DT>(b.x & 0xFFFFu), from_bits16<DT>(b.x >> 16),
+                     from_bits16<DT>(b.y & 0xFFFFu), from_bits16<DT>(b.y >> 16));
+}
+
+template <int DT>
+__device__ __forceinline__ void store4(void* base, int64_t i, const float4& v) {
+  if (DT == DFC_DTYPE_F32) {
+    __stcs(reinterpret_cast<float4*>(static_cast<float*>(base) + i), v);
+  } else {
+    const uint2 b = make_uint2(to_bits16<DT>(v.x) | (to_bits16<DT>(v.y) << 16),
+                               to_bits16<DT>(v.z) | (to_bits16<DT>(v.w) << 16));
+    __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + i), b);
   }
-  return __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(g) + i));
 }
 
-template <bool BF16>
-__device__ __forceinline__ float load_grad1(const void* g, int64_t i) {
-  if (BF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(g)[i]);
-  return static_cast<const float*>(g)[i];
+template <int DT>
+__device__ __forceinline__ float load1(const void* base, int64_t i) {
+  if (DT == DFC_DTYPE_F32) return static_cast<const float*>(base)[i];
+  return from_bits16<DT>(static_cast<const uint16_t*>(base)[i]);
 }
 
-template <int MODE>
+template <int DT>
+__device__ __forceinline__ void store1(void* base, int64_t i, float v) {
+  if (DT == DFC_DTYPE_F32) static_cast<float*>(base)[i] = v;
+  else static_cast<uint16_t*>(base)[i] = static_cast<uint16_t>(to_bits16<DT>(v));
+}
+
+template <int MODE, int PDT>
 __device__ __forceinline__ void step4(const Scalars& s, float4& P, const float4& G, uint4& M,
                                       uint4& V) {
-  step_elem<MODE>(s, P.x, G.x, M.x, V.x);
-  step_elem<MODE>(s, P.y, G.y, M.y, V.y);
-  step_elem<MODE>(s, P.z, G.z, M.z, V.z);
-  step_elem<MODE>(s, P.w, G.w, M.w, V.w);
+  step_elem<MODE, PDT>(s, P.x, G.x, M.x, V.x);
+  step_elem<MODE, PDT>(s, P.y, G.y, M.y, V.y);
+  step_elem<MODE, PDT>(s, P.z, G.z, M.z, V.z);
+  step_elem<MODE, PDT>(s, P.w, G.w, M.w, V.w);
 }
 
-template <int MODE, bool BF16>
+template <int MODE, int GDT, int PDT>
 __device__ __forceinline__ void tile_full_vec(const SegArg& sg, int64_t base, const Scalars& s) {
   float4 P[kUnroll], G[kUnroll];
   uint4 M[kUnroll], V[kUnroll];
 #pragma unroll
   for (int u = 0; u < kUnroll; ++u) {
     const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
-    P[u] = __ldcs(reinterpret_cast<const float4*>(sg.p + i));
-    G[u] = load_grad4<BF16>(sg.g, i);
+    P[u] = load4<PDT>(sg.p, i);
+    G[u] = load4<GDT>(sg.g, i);
     M[u] = __ldcs(reinterpret_cast<const uint4*>(sg.m + i));
     V[u] = __ldcs(reinterpret_cast<const uint4*>(sg.v + i));
   }
 #pragma unroll
   for (int u = 0; u < kUnroll; ++u) {
     const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
-    step4<MODE>(s, P[u], G[u], M[u], V[u]);
-    __stcs(reinterpret_cast<float4*>(sg.p + i), P[u]);
+    step4<MODE, PDT>(s, P[u], G[u], M[u], V[u]);
+    store4<PDT>(sg.p, i, P[u]);
     __stcs(reinterpret_cast<uint4*>(sg.m + i), M[u]);
     __stcs(reinterpret_cast<uint4*>(sg.v + i), V[u]);
   }
 }
 
-template <int MODE, bool BF16>
+template <int MODE, int GDT, int PDT>
 __device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int64_t count,
                                              bool vec, const Scalars& s) {
   int64_t done = 0;
@@ -126,12 +143,12 @@ __device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int
     const int64_t nv = count / kVec;
     for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
       const int64_t i = base + j * kVec;
-      float4 P = __ldcs(reinterpret_cast<const float4*>(sg.p + i));
-      const float4 G = load_grad4<BF16>(sg.g, i);
+      float4 P = load4<PDT>(sg.p, i);
+      const float4 G = load4<GDT>(sg.g, i);
       uint4 M = __ldcs(reinterpret_cast<const uint4*>(sg.m + i));
       uint4 V = __ldcs(reinterpret_cast<const uint4*>(sg.v + i));
-      step4<MODE>(s, P, G, M, V);
-      __stcs(reinterpret_cast<float4*>(sg.p + i), P);
+      step4<MODE, PDT>(s, P, G, M, V);
+      store4<PDT>(sg.p, i, P);
       __stcs(reinterpret_cast<uint4*>(sg.m + i), M);
       __stcs(reinterpret_cast<uint4*>(sg.v + i), V);
     }
@@ -139,16 +156,27 @@ __device__ __forceinline__ void tile_partial(const SegArg& sg, int64_t base, int
   }
   for (int64_t j = done + threadIdx.x; j < count; j += kThreads) {
     const int64_t i = base + j;
-    float p = sg.p[i];
+    float p = load1<PDT>(sg.p, i);
     uint32_t m = sg.m[i], v = sg.v[i];
-    step_elem<MODE>(s, p, load_grad1<BF16>(sg.g, i), m, v);
-    sg.p[i] = p;
+    step_elem<MODE, PDT>(s, p, load1<GDT>(sg.g, i), m, v);
+    store1<PDT>(sg.p, i, p);
     sg.m[i] = m;
     sg.v[i] = v;
   }
 }
 
-template <int MODE, int MAXS, int MAXH>
+template <int MODE, int GDT, int PDT>
+__device__ __forceinline__ void run_tile(const SegArg& sg, int64_t base, int64_t count,
+                                         const Scalars& s) {
+  const bool vec = (sg.flags & kFlagVec) != 0;
+  if (vec && count == kTile) tile_full_vec<MODE, GDT, PDT>(sg, base, s);
+  else tile_partial<MODE, GDT, PDT>(sg, base, count, vec, s);
+}
+
+// One kernel per (moment format, gradient type, parameter type): a launch
+// holds segments of a single type combination, so the hot FP32 kernel keeps
+// its 32-register budget.
+template <int MODE, int GDT, int PDT, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, DFC_STEP_MIN_BLOCKS)
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
   const int32_t t = static_cast<int32_t>(blockIdx.x);
@@ -159,47 +187,53 @@ __global__ void __launch_bounds__(kThreads, DFC_STEP_MIN_BLOCKS)
   }
   const SegArg& sg = b.seg[lo];
   const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
-
   const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
   const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
-  const bool vec = (sg.flags & kFlagVec) != 0;
-  if (sg.flags & kFlagBf16) {
-    if (vec && count == kTile) tile_full_vec<MODE, true>(sg, base, s);
-    else tile_partial<MODE, true>(sg, base, count, vec, s);
-  } else {
-    if (vec && count == kTile) tile_full_vec<MODE, false>(sg, base, s);
-    else tile_partial<MODE, false>(sg, base, count, vec, s);
+  run_tile<MODE, GDT, PDT>(sg, base, count, s);
+}
+
+// type combination code: gradient type | parameter type << 2
+int32_t types_of(const DfcSegment& s) { return s.grad_dtype | (s.param_dtype << 2); }
+
+template <int MODE, int MAXS, int MAXH>
+void launch_types(const StepBatch<MAXS, MAXH>& b, int32_t types, int32_t grid, cudaStream_t st) {
+  switch (types) {
+    case 0: step_kernel<MODE, 0, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 1: step_kernel<MODE, 1, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 2: step_kernel<MODE, 2, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 4: step_kernel<MODE, 0, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 5: step_kernel<MODE, 1, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 6: step_kernel<MODE, 2, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 8: step_kernel<MODE, 0, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 9: step_kernel<MODE, 1, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    default: step_kernel<MODE, 2, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
   }
 }
 
 template <int MAXS, int MAXH>
-int launch_batch(StepBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
+int launch_batch(StepBatch<MAXS, MAXH>& b, int32_t mode, int32_t types, cudaStream_t st) {
   const int32_t tiles = b.tile_base[b.n_segs];
   if (tiles == 0) return DFC_OK;
-  const int32_t grid = tiles;
   switch (mode) {
-    case DFC_MODE_PLAIN:
-      step_kernel<DFC_MODE_PLAIN, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b);
-      break;
-    case DFC_MODE_SIGNFIBER:
-      step_kernel<DFC_MODE_SIGNFIBER, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b);
-      break;
-    default:
-      step_kernel<DFC_MODE_PACKED, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b);
-      break;
+    case DFC_MODE_PLAIN: launch_types<DFC_MODE_PLAIN>(b, types, tiles, st); break;
+    case DFC_MODE_SIGNFIBER: launch_types<DFC_MODE_SIGNFIBER>(b, types, tiles, st); break;
+    default: launch_types<DFC_MODE_PACKED>(b, types, tiles, st); break;
   }
   return launch_status();
 }
+
+bool valid_dtype(int32_t t) { return t == DFC_DTYPE_F32 || t == DFC_DTYPE_BF16 || t == DFC_DTYPE_F16; }
+
+uintptr_t elem_size(int32_t t) { return t == DFC_DTYPE_F32 ? 4 : 2; }
 
 int validate(const DfcSegment& s, int32_t n_hypers) {
   if (s.numel < 0) return DFC_ERR_SIZE;
   if (s.numel == 0) return DFC_OK;
   if (!s.param || !s.grad || !s.exp_avg || !s.exp_avg_sq) return DFC_ERR_NULL;
   if (s.hyper < 0 || s.hyper >= n_hypers) return DFC_ERR_HYPER;
-  if (s.grad_dtype != DFC_GRAD_F32 && s.grad_dtype != DFC_GRAD_BF16) return DFC_ERR_DTYPE;
-  const uintptr_t ga = s.grad_dtype == DFC_GRAD_BF16 ? 2 : 4;
-  if (!aligned(s.param, 4) || !aligned(s.exp_avg, 4) || !aligned(s.exp_avg_sq, 4) ||
-      !aligned(s.grad, ga))
+  if (!valid_dtype(s.grad_dtype) || !valid_dtype(s.param_dtype)) return DFC_ERR_DTYPE;
+  if (!aligned(s.param, elem_size(s.param_dtype)) || !aligned(s.exp_avg, 4) ||
+      !aligned(s.exp_avg_sq, 4) || !aligned(s.grad, elem_size(s.grad_dtype)))
     return DFC_ERR_ALIGN;
   if ((s.numel + kTile - 1) / kTile > INT32_MAX / 2) return DFC_ERR_SIZE;
   return DFC_OK;
@@ -213,19 +247,19 @@ SegArg to_arg(const DfcSegment& s, int32_t local_hyper) {
   a.v = s.exp_avg_sq;
   a.n = s.numel;
   a.hyper = local_hyper;
-  const bool bf16 = s.grad_dtype == DFC_GRAD_BF16;
-  const bool vec = aligned(s.param, 16) && aligned(s.exp_avg, 16) && aligned(s.exp_avg_sq, 16) &&
-                   aligned(s.grad, bf16 ? 8 : 16);
-  a.flags = (bf16 ? kFlagBf16 : 0) | (vec ? kFlagVec : 0);
+  // a vector of four elements: 16 bytes of FP32, 8 bytes of a 16-bit type
+  const bool vec = aligned(s.param, 4 * elem_size(s.param_dtype)) && aligned(s.exp_avg, 16) &&
+                   aligned(s.exp_avg_sq, 16) && aligned(s.grad, 4 * elem_size(s.grad_dtype));
+  a.flags = vec ? kFlagVec : 0;
   return a;
 }
 
-// Pack segments into as few launches as the per-launch capacity allows.  A
-// batch closes when it holds MAXS segments, MAXH distinct hyper sets, or
-// would pass INT32_MAX tiles.
+// Pack the segments of one type combination into as few launches as the
+// per-launch capacity allows.  A batch closes when it holds MAXS segments,
+// MAXH distinct hyper sets, or would pass INT32_MAX tiles.
 template <int MAXS, int MAXH>
 int run_batches(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32_t n_hypers,
-                int32_t mode, const float* dscale, cudaStream_t st) {
+                int32_t mode, int32_t types, const float* dscale, cudaStream_t st) {
   StepBatch<MAXS, MAXH> b;
   std::vector<int32_t> local(static_cast<size_t>(n_hypers), -1);
   std::vector<int32_t> used;
@@ -239,12 +273,12 @@ int run_batches(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32
   reset();
   for (int32_t i = 0; i < n; ++i) {
     const DfcSegment& s = segs[i];
-    if (s.numel == 0) continue;
+    if (s.numel == 0 || types_of(s) != types) continue;
     const int32_t tiles = static_cast<int32_t>((s.numel + kTile - 1) / kTile);
     const bool need_hyper = local[s.hyper] < 0;
     if (b.n_segs == MAXS || (need_hyper && static_cast<int>(used.size()) == MAXH) ||
         b.tile_base[b.n_segs] > INT32_MAX - tiles) {
-      int rc = launch_batch(b, mode, st);
+      int rc = launch_batch(b, mode, types, st);
       if (rc != DFC_OK) return rc;
       reset();
     }
@@ -257,7 +291,21 @@ int run_batches(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32
     b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
     ++b.n_segs;
   }
-  return b.n_segs ? launch_batch(b, mode, st) : DFC_OK;
+  return b.n_segs ? launch_batch(b, mode, types, st) : DFC_OK;
+}
+
+template <int MAXS, int MAXH>
+int run_all(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32_t n_hypers,
+            int32_t mode, const float* dscale, cudaStream_t st) {
+  bool present[16] = {};
+  for (int32_t i = 0; i < n; ++i)
+    if (segs[i].numel > 0) present[types_of(segs[i])] = true;
+  for (int32_t types = 0; types < 16; ++types) {
+    if (!present[types]) continue;
+    const int rc = run_batches<MAXS, MAXH>(segs, n, hypers, n_hypers, mode, types, dscale, st);
+    if (rc != DFC_OK) return rc;
+  }
+  return DFC_OK;
 }
 
 // ---- moment-format conversion -------------------------------------------
@@ -307,10 +355,10 @@ extern "C" int dfc_mt_step(const DfcSegment* segments, int32_t n_segments, const
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (n_segments <= kSmallSegs && n_hypers <= kSmallHypers)
-    return run_batches<kSmallSegs, kSmallHypers>(segments, n_segments, hypers, n_hypers, mode,
-                                                 device_grad_scale, st);
-  return run_batches<kLargeSegs, kLargeHypers>(segments, n_segments, hypers, n_hypers, mode,
-                                               device_grad_scale, st);
+    return run_all<kSmallSegs, kSmallHypers>(segments, n_segments, hypers, n_hypers, mode,
+                                             device_grad_scale, st);
+  return run_all<kLargeSegs, kLargeHypers>(segments, n_segments, hypers, n_hypers, mode,
+                                           device_grad_scale, st);
 }
 
 extern "C" int dfc_pack_moments(uint32_t* words, int64_t n, int32_t second, void* stream) {

@@ -10,15 +10,47 @@
 // Packed words: decoded before and re-encoded after with integer bit ops.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "dfc_common.cuh"
 
 namespace dfc {
+
+// ---- 16-bit parameter types ----------------------------------------------
+// Round to nearest even; a NaN becomes the type's canonical quiet NaN (bf16
+// 0x7FC0, fp16 0x7E00), as PyTorch's CPU conversions produce.
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float x) {
+  const uint32_t b = f2u(x);
+  return (b & 0x7FFFFFFFu) > 0x7F800000u ? 0x7FC0u : (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
+}
+
+__device__ __forceinline__ uint32_t f32_to_f16_bits(float x) {
+  return x != x ? 0x7E00u : static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x)));
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t to_bits16(float x) {
+  return DT == DFC_DTYPE_BF16 ? f32_to_bf16_bits(x) : f32_to_f16_bits(x);
+}
+
+template <int DT>
+__device__ __forceinline__ float from_bits16(uint32_t h) {
+  return DT == DFC_DTYPE_BF16 ? u2f(h << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+// x rounded to the parameter type (identity for FP32)
+template <int DT>
+__device__ __forceinline__ float round_to(float x) {
+  return DT == DFC_DTYPE_F32 ? x : from_bits16<DT>(to_bits16<DT>(x));
+}
 
 struct Scalars {
   float b1, omb1, b2, omb2, sbc2, eps, decay, nstep, gscale, dscale;
 };
 
-template <int MODE>
+// p holds the parameter's value as FP32 (exact for 16-bit types) and comes
+// back rounded to PDT.
+template <int MODE, int PDT = DFC_DTYPE_F32>
 __device__ __forceinline__ void step_elem(const Scalars& s, float& p, float gin, uint32_t& mw,
                                           uint32_t& vw) {
   const float g = __fmul_rn(__fmul_rn(gin, s.gscale), s.dscale);
@@ -48,8 +80,14 @@ __device__ __forceinline__ void step_elem(const Scalars& s, float& p, float gin,
     vw = payload | (MODE == DFC_MODE_PACKED ? enc_mag(mag) : mag);
   }
   const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(v_upd), s.sbc2), s.eps);
-  const float upd = __fdiv_rn(__fmul_rn(s.nstep, m_new), den);
-  p = __fadd_rn(__fmul_rn(p, s.decay), upd);
+  if (PDT == DFC_DTYPE_F32) {
+    const float upd = __fdiv_rn(__fmul_rn(s.nstep, m_new), den);
+    p = __fadd_rn(__fmul_rn(p, s.decay), upd);
+  } else {
+    const float p1 = round_to<PDT>(__fmul_rn(p, s.decay));
+    const float upd = __fdiv_rn(__fmul_rn(s.nstep, round_to<PDT>(m_new)), round_to<PDT>(den));
+    p = round_to<PDT>(__fadd_rn(p1, upd));
+  }
   mw = MODE == DFC_MODE_PACKED ? pack_signed(m_new) : f2u(m_new);
 }
 

@@ -14,7 +14,9 @@ import torch
 
 from . import _lib
 
-_GRAD_CODES = {torch.float32: _lib.GRAD_F32, torch.bfloat16: _lib.GRAD_BF16}
+DTYPE_CODES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+               torch.float16: _lib.DTYPE_F16}
+_GRAD_CODES = DTYPE_CODES
 
 
 def _stream(dev: torch.device) -> int:
@@ -47,17 +49,18 @@ def segments(params: Sequence[torch.Tensor], grads: Sequence[torch.Tensor],
     segs = np.zeros(n, dtype=_lib.SEGMENT_DTYPE)
     for i in range(n):
         p, g, m, v = params[i], grads[i], _words(exp_avgs[i]), _words(exp_avg_sqs[i])
-        if p.dtype != torch.float32:
-            raise TypeError("parameters must be FP32")
-        code = _GRAD_CODES.get(g.dtype)
+        pcode = DTYPE_CODES.get(p.dtype)
+        if pcode is None:
+            raise TypeError("parameters must be FP32, bf16 or fp16")
+        code = DTYPE_CODES.get(g.dtype)
         if code is None:
-            raise TypeError("gradients must be FP32 or bf16")
+            raise TypeError("gradients must be FP32, bf16 or fp16")
         if not (p.numel() == g.numel() == m.numel() == v.numel()):
             raise ValueError("segment tensors differ in size")
         if not (p.is_contiguous() and g.is_contiguous() and m.is_contiguous() and v.is_contiguous()):
             raise ValueError("segment tensors must be contiguous")
         segs[i] = (p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(),
-                   int(hyper_index[i]), code)
+                   int(hyper_index[i]), code, pcode)
     return segs
 
 
@@ -128,9 +131,9 @@ def compress_ef(grad: torch.Tensor, comp: torch.Tensor, resid: torch.Tensor) -> 
 def grad_refs(grads: Sequence[torch.Tensor]) -> np.ndarray:
     refs = np.zeros(len(grads), dtype=_lib.GRADREF_DTYPE)
     for i, g in enumerate(grads):
-        code = _GRAD_CODES.get(g.dtype)
+        code = DTYPE_CODES.get(g.dtype)
         if code is None:
-            raise TypeError("gradients must be FP32 or bf16")
+            raise TypeError("gradients must be FP32, bf16 or fp16")
         if not g.is_contiguous():
             raise ValueError("gradients must be contiguous")
         refs[i] = (g.data_ptr(), g.numel(), code, 0)

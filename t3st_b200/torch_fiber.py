@@ -32,6 +32,11 @@ MAGNITUDE_MASK_I32 = 2147483647
 
 _FORMATS = ("fp32", "packed")
 
+# parameter and gradient types the kernels read and write directly; other
+# floating gradients are converted with .float() (remote/torch_fiber.py:83)
+_PARAM_CODES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+                torch.float16: _lib.DTYPE_F16}
+
 
 def _is_dense(t: torch.Tensor) -> bool:
     """True when t's elements occupy one gap-free block of memory in some
@@ -258,25 +263,25 @@ class DFCAdamW(torch.optim.Optimizer):
             if not p.is_cuda:
                 raise RuntimeError("DFCAdamW (t3st_b200) runs on CUDA tensors only; "
                                    "move the model to a CUDA device")
-            if p.dtype != torch.float32:
-                raise NotImplementedError("DFCAdamW (t3st_b200) updates FP32 parameters")
+            pcode = _PARAM_CODES.get(p.dtype)
+            if pcode is None:
+                raise TypeError("DFCAdamW expects floating parameters")
             if g.device != p.device or g.shape != p.shape:
                 raise RuntimeError("gradient must match its parameter's device and shape")
             m, v = state["exp_avg"], state["exp_avg_sq"]
             if not _is_dense(p):
                 raise RuntimeError("DFCAdamW (t3st_b200) needs dense parameters")
-            if g.dtype == torch.bfloat16:
-                code = _lib.GRAD_BF16
-            else:
-                code = _lib.GRAD_F32
-                if g.dtype != torch.float32:
-                    g = g.float()  # remote/torch_fiber.py:83
+            code = _PARAM_CODES.get(g.dtype)
+            if code is None:
+                g = g.float()  # remote/torch_fiber.py:83
+                code = _lib.DTYPE_F32
             if g.stride() != p.stride():
                 g = torch.empty_like(p, dtype=g.dtype).copy_(g)
             if m.stride() != p.stride() or v.stride() != p.stride():
                 raise RuntimeError("optimizer state layout differs from its parameter")
             keep.append(g)
-            segs[i] = (p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), 0, code)
+            segs[i] = (p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), 0, code,
+                       pcode)
             if i + 1 == len(work) or work[i + 1][0].device != p.device:
                 devices.append((p.device, slice(start, i + 1)))
                 start = i + 1

@@ -29,6 +29,9 @@ Cases (all FP32):
                  wd 0 (the reference skips the decay), betas (0.8, 0.95), eps 1e-6.
   c1_small       one 2^14 tensor, 12 steps, p~N(0,0.02), g~N(0,1e-3), lr 1e-3,
                  betas (0.9,0.999), eps 1e-8, wd 0.01, random payload.
+  bf16_params,   3 bf16 (or fp16) parameter tensors (1031, 300, 7) with
+  f16_params     gradients of the same type, 6 steps, payload, lr 1e-3, wd 0.01;
+                 p is stored as the 16-bit patterns.
   unit_linear    the reference's own unit-test trajectory
                  (remote/test_torch_fiber.py:11-31): Linear(257,31), seed 17,
                  50 steps of MSE, lr 3e-4, wd 0.01; final params of the
@@ -201,6 +204,49 @@ def case_c1(tf):
          **group_arrays(group))
 
 
+def case_lowp(tf, dtype, name):
+    rng = np.random.default_rng(4004)
+    sizes = [1031, 300, 7]
+    total = sum(sizes)
+    steps = 6
+    p0 = torch.from_numpy((rng.standard_normal(total) * 0.02).astype(np.float32)).to(dtype)
+    grads = torch.from_numpy((rng.standard_normal((steps, total)) * 1e-3).astype(np.float32)).to(dtype)
+    payload = rng.integers(0, 2, total, dtype=np.uint8)
+    group = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+
+    def run():
+        params, off = [], 0
+        for n in sizes:
+            params.append(torch.nn.Parameter(p0[off:off + n].clone()))
+            off += n
+        opt = tf.DFCAdamW(params, **group, enable_fiber=True)
+        tf.TorchSignFiberChannel(opt).write_bits(0, payload)
+        for s in range(steps):
+            off = 0
+            for p, n in zip(params, sizes):
+                p.grad = grads[s, off:off + n].clone()
+                off += n
+            opt.step()
+        p = torch.cat([q.detach().reshape(-1) for q in params]).view(torch.int16).numpy().view(np.uint16)
+        m = np.concatenate([opt.state[q]["exp_avg"].reshape(-1).numpy() for q in params]).view(np.uint32)
+        v = np.concatenate([opt.state[q]["exp_avg_sq"].reshape(-1).view(torch.int32).numpy()
+                            for q in params]).view(np.uint32)
+        return p.copy(), m.copy(), v.copy()
+
+    p, m, v = run()
+    torch.Tensor.sqrt = _ieee_sqrt
+    try:
+        pi, m2, v2 = run()
+    finally:
+        torch.Tensor.sqrt = _stock_sqrt
+    assert np.array_equal(m, m2) and np.array_equal(v, v2)
+    save(name, sizes=np.array(sizes, np.int64),
+         p0=p0.view(torch.int16).numpy().view(np.uint16), grads=grads.view(torch.int16).numpy().view(np.uint16),
+         none_mask=np.zeros((steps, len(sizes)), bool), fiber=np.bool_(True), payload=payload,
+         p=p, p_ieee_sqrt=pi, m=m, v=v, steps=np.full(len(sizes), steps, np.int64),
+         dtype=np.array("bf16" if dtype == torch.bfloat16 else "f16"), **group_arrays(group))
+
+
 def case_unit_linear(tf):
     torch.manual_seed(17)
     reference = torch.nn.Linear(257, 31)
@@ -244,6 +290,8 @@ def main():
     case_mt(tf, False, "plain_mt")
     case_ragged(tf, oracle)
     case_c1(tf)
+    case_lowp(tf, torch.bfloat16, "bf16_params")
+    case_lowp(tf, torch.float16, "f16_params")
     case_unit_linear(tf)
 
 

@@ -11,6 +11,11 @@ from oracle import oracle as O
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = ("fiber_mt", "plain_mt", "ragged_stress", "c1_small")
+LOWP_CASES = ("bf16_params", "f16_params")
+
+
+def param_dtype(d) -> str:
+    return str(d["dtype"]) if "dtype" in d else "f32"
 
 
 def load(name: str) -> dict:
@@ -54,8 +59,23 @@ def oracle_replay(d, mode: int):
     grads = d["grads"]
     for s in range(grads.shape[0]):
         gl = [None if d["none_mask"][s, i] else grads[s, off[i]:off[i + 1]] for i in range(n)]
-        O.multi_tensor_step(mode, ts, gl, group_of(d), steps)
+        O.multi_tensor_step(mode, ts, gl, group_of(d), steps, param_dtype=param_dtype(d))
     return p, m, v, np.array(steps, np.int64)
+
+
+def lowp_to_f32(bits: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "bf16":
+        return (bits.astype(np.uint32) << 16).view(np.float32)
+    return bits.view(np.float16).astype(np.float32)
+
+
+def lowp_ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in ulps of the 16-bit type, on the monotone integer line."""
+    ai = a.view(np.int16).astype(np.int64)
+    bi = b.view(np.int16).astype(np.int64)
+    ai = np.where(ai < 0, -(ai & 0x7FFF), ai)
+    bi = np.where(bi < 0, -(bi & 0x7FFF), bi)
+    return np.abs(ai - bi)
 
 
 def expected_words(d, packed: bool):

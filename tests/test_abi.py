@@ -49,7 +49,7 @@ def test_struct_sizes_match_header():
 
 def _seg(**kw):
     s = np.zeros(1, dtype=_lib.SEGMENT_DTYPE)
-    s[0] = (0x10000, 0x20000, 0x30000, 0x40000, 16, 0, 0)
+    s[0] = (0x10000, 0x20000, 0x30000, 0x40000, 16, 0, 0, 0)
     for k, v in kw.items():
         s[0][k] = v
     return s
@@ -69,7 +69,9 @@ def test_step_rejects_bad_arguments_before_launch():
         (_seg(grad=0), _lib.DFC_ERR_NULL),
         (_seg(hyper=1), _lib.DFC_ERR_HYPER),
         (_seg(hyper=-1), _lib.DFC_ERR_HYPER),
-        (_seg(grad_dtype=2), _lib.DFC_ERR_DTYPE),
+        (_seg(grad_dtype=3), _lib.DFC_ERR_DTYPE),
+        (_seg(param_dtype=7), _lib.DFC_ERR_DTYPE),
+        (_seg(param=0x10001, param_dtype=1), _lib.DFC_ERR_ALIGN),
         (_seg(param=0x10002), _lib.DFC_ERR_ALIGN),
         (_seg(exp_avg_sq=0x40001), _lib.DFC_ERR_ALIGN),
         (_seg(grad=0x20002), _lib.DFC_ERR_ALIGN),

@@ -15,12 +15,28 @@ from t3st_b200 import DFCAdamW
 pytestmark = pytest.mark.gpu
 
 
+TORCH_DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def _to_torch(a, dt):
+    if dt == "f32":
+        return torch.from_numpy(a.copy())
+    return torch.from_numpy(a.view(np.int16).copy()).view(TORCH_DT[dt])
+
+
+def _to_numpy(t):
+    t = t.detach().reshape(-1).cpu()
+    if t.dtype == torch.float32:
+        return t.numpy()
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
 def run_ours(d, fmt, dev):
     off = G.offsets(d)
     n = len(d["sizes"])
+    dt = G.param_dtype(d)
     p0, m0, v0 = G.initial_state(d, packed=fmt == "packed")
-    params = [torch.nn.Parameter(torch.from_numpy(p0[off[i]:off[i + 1]].copy()).to(dev))
-              for i in range(n)]
+    params = [torch.nn.Parameter(_to_torch(p0[off[i]:off[i + 1]], dt).to(dev)) for i in range(n)]
     group = G.group_of(d)
     opt = DFCAdamW(params, lr=group["lr"], betas=group["betas"], eps=group["eps"],
                    weight_decay=group["weight_decay"], enable_fiber=bool(d["fiber"]),
@@ -29,13 +45,13 @@ def run_ours(d, fmt, dev):
         st = opt.state[p]
         st["exp_avg"].view(torch.int32).copy_(torch.from_numpy(m0[off[i]:off[i + 1]].view(np.int32)))
         st["exp_avg_sq"].view(torch.int32).copy_(torch.from_numpy(v0[off[i]:off[i + 1]].view(np.int32)))
-    grads = torch.from_numpy(d["grads"]).to(dev)
+    grads = _to_torch(d["grads"], dt).to(dev)
     for s in range(grads.shape[0]):
         for i, p in enumerate(params):
             p.grad = None if d["none_mask"][s, i] else grads[s, off[i]:off[i + 1]].clone()
         opt.step()
     torch.cuda.synchronize()
-    p = torch.cat([x.detach().reshape(-1) for x in params]).cpu().numpy()
+    p = np.concatenate([_to_numpy(x) for x in params])
     m = torch.cat([opt.state[x]["exp_avg"].reshape(-1) for x in params]).cpu().numpy().view(np.uint32)
     v = torch.cat([opt.state[x]["exp_avg_sq"].reshape(-1) for x in params]).cpu().numpy().view(np.uint32)
     steps = np.array([opt.state[x]["step"] for x in params])
@@ -58,3 +74,17 @@ def test_step_matches_reference(name, fmt, cuda):
     np.testing.assert_array_equal(p.view(np.uint32), d["p_ieee_sqrt"].view(np.uint32))
     ok, worst = G.p_matches_stock(p, d)
     assert ok, worst
+
+
+@pytest.mark.parametrize("name", G.LOWP_CASES)
+@pytest.mark.parametrize("fmt", ["fp32", "packed"])
+def test_reduced_precision_params_match_reference(name, fmt, cuda):
+    d = G.load(name)
+    p, m, v, steps = run_ours(d, fmt, cuda)
+    np.testing.assert_array_equal(steps, d["steps"])
+    em, ev = G.expected_words(d, fmt == "packed")
+    np.testing.assert_array_equal(m, em)
+    np.testing.assert_array_equal(v, ev)
+    np.testing.assert_array_equal(p, d["p_ieee_sqrt"])
+    ulp = G.lowp_ulp_distance(p, d["p"])
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.02

@@ -3,6 +3,8 @@ random inputs: every moment format, FP32 and bf16 gradients, ragged and
 misaligned segments, several hyper sets, the multi-launch batching, special
 values, and the device-side gradient scale."""
 
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -209,3 +211,62 @@ def test_public_step_fast_path_follows_storage_and_grad_changes(cuda):
         np.testing.assert_array_equal(opt.state[p]["exp_avg"].cpu().numpy().view(np.uint32), r["m"])
         np.testing.assert_array_equal(opt.state[p]["exp_avg_sq"].cpu().numpy().view(np.uint32), r["v"])
     assert [opt.state[p]["step"] for p in params] == steps == [12, 11, 12]
+
+
+NPDT = {"f32": (np.float32, torch.float32), "bf16": (np.uint16, torch.bfloat16),
+        "f16": (np.uint16, torch.float16)}
+
+
+def _lowp_bits(x, dt):
+    if dt == "f32":
+        return x.astype(np.float32)
+    t = torch.from_numpy(x.astype(np.float32)).to(NPDT[dt][1])
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("pdt", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("gdt", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("mode", [O.MODE_SIGNFIBER, O.MODE_PACKED])
+def test_parameter_and_gradient_types(cuda, pdt, gdt, mode):
+    """Every (gradient type, parameter type) pair against the oracle, bit for
+    bit, aligned and misaligned, with several sizes in one call."""
+    rng = np.random.default_rng(zlib.crc32(f"{pdt}{gdt}{mode}".encode()))
+    sizes = [1, 3, 4099, 1024, 33, 70000]
+    h = O.reference_hyper(1e-3, (0.9, 0.999), 1e-8, 0.01, 4)
+    host, keep = [], []
+    segs = np.zeros(len(sizes), dtype=_lib.SEGMENT_DTYPE)
+    codes = {"f32": _lib.DTYPE_F32, "bf16": _lib.DTYPE_BF16, "f16": _lib.DTYPE_F16}
+    for k, n in enumerate(sizes):
+        off = k % 3
+        p = _lowp_bits(rng.standard_normal(n) * 0.02, pdt)
+        g = _lowp_bits(rng.standard_normal(n) * 1e-3, gdt)
+        m = (rng.standard_normal(n) * 1e-4).astype(np.float32).view(np.uint32)
+        v = (np.abs(rng.standard_normal(n)) * 1e-7).astype(np.float32).view(np.uint32)
+        v |= rng.integers(0, 2, n, dtype=np.uint32) << 31
+        if mode == O.MODE_PACKED:
+            m = O.pack_first(m.view(np.float32))
+            v = O.pack_second(v)
+
+        def put(a, tdt):
+            buf = torch.zeros(n + off + 8, dtype=tdt, device=cuda)
+            t = buf[off:off + n]
+            src = torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a.copy())
+            t.view(src.dtype).copy_(src)
+            return t
+
+        tp = put(p, NPDT[pdt][1])
+        tg = put(g, NPDT[gdt][1])
+        tm = put(m.view(np.int32), torch.int32)
+        tv = put(v.view(np.int32), torch.int32)
+        keep.append((tp, tg, tm, tv))
+        host.append((p.copy(), g, m.copy(), v.copy()))
+        segs[k] = (tp.data_ptr(), tg.data_ptr(), tm.data_ptr(), tv.data_ptr(), n, 0, codes[gdt],
+                   codes[pdt])
+    kernels.mt_step_raw(segs, kernels.hypers([_row_tuple(h)]), mode, cuda)
+    torch.cuda.synchronize()
+    for (p, g, m, v), (tp, tg, tm, tv) in zip(host, keep):
+        O.step(mode, h, p, g, m, v, param_dtype=pdt, grad_dtype=gdt)
+        got_p = tp.cpu().view(torch.int16).numpy().view(np.uint16) if pdt != "f32" else tp.cpu().numpy()
+        np.testing.assert_array_equal(got_p.view(p.dtype), p)
+        np.testing.assert_array_equal(tm.cpu().numpy().view(np.uint32), m)
+        np.testing.assert_array_equal(tv.cpu().numpy().view(np.uint32), v)

@@ -51,3 +51,20 @@ def test_per_tensor_step_counters():
     assert list(d["steps"]) == [6, 6, 5, 6]
     d = G.load("ragged_stress")
     assert d["steps"][0] == 3 and d["steps"][5] == 3 and d["steps"][1] == 4
+
+
+@pytest.mark.parametrize("name", G.LOWP_CASES)
+@pytest.mark.parametrize("mode", [O.MODE_SIGNFIBER, O.MODE_PACKED])
+def test_oracle_reduced_precision_params(name, mode):
+    """bf16/fp16 parameters (remote/torch_fiber.py:45, 114-116): FP32 moments
+    bit-exact, parameters bit-exact against the IEEE-sqrt reference; against
+    the stock reference a few elements are one ulp of the 16-bit type off."""
+    d = G.load(name)
+    p, m, v, steps = G.oracle_replay(d, mode)
+    np.testing.assert_array_equal(steps, d["steps"])
+    em, ev = G.expected_words(d, mode == O.MODE_PACKED)
+    np.testing.assert_array_equal(m, em)
+    np.testing.assert_array_equal(v, ev)
+    np.testing.assert_array_equal(p, d["p_ieee_sqrt"])
+    ulp = G.lowp_ulp_distance(p, d["p"])
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.02
