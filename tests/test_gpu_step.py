@@ -91,7 +91,7 @@ def _run_case(dev, sizes, mode, bf16, n_hypers, offset_elems, seed, specials=Fal
     segs = np.zeros(len(sizes), dtype=_lib.SEGMENT_DTYPE)
     for k, (tp, tg, tm, tv) in enumerate(dev_tensors):
         segs[k] = (tp.data_ptr(), tg.data_ptr(), tm.data_ptr(), tv.data_ptr(), sizes[k],
-                   k % n_hypers, _lib.GRAD_BF16 if bf16 else _lib.GRAD_F32)
+                   k % n_hypers, _lib.GRAD_BF16 if bf16 else _lib.GRAD_F32, _lib.DTYPE_F32)
     hyp = kernels.hypers([_row_tuple(h) for h in hs])
     dscale = None
     if scale is not None:
