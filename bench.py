@@ -60,9 +60,9 @@ def parse_args():
                     help="skip the nvidia-smi clock sampler (profiling runs)")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
-    ap.add_argument("--transport", choices=("auto", "peer", "nccl"), default="auto",
-                    help="N>1: fused kernel over NVLink peer memory, NCCL collectives, or "
-                         "the measured faster of the two for N (peer at 2 ranks)")
+    ap.add_argument("--transport", choices=("auto", "peer", "nvls", "nccl"), default="auto",
+                    help="N>1: fused kernel over NVLink peer memory, the same kernel over "
+                         "NVSwitch multicast, NCCL collectives, or the measured fastest for N")
     return ap.parse_args()
 
 
@@ -502,7 +502,12 @@ def run_sharded(args, rank, world, device):
     value = P * K / (ms / 1e3)
     # roofline: the slower of this rank's HBM bytes and its NVLink bytes
     hbm_bytes = 12 * P + 26 * P // world          # compress over P, step over the shard
-    nvl_bytes = 6 * P * (world - 1) // world      # bf16 RS + FP32 AG, per direction
+    if opt.transport == "nvls":
+        # in: the reduced bf16 piece + every rank's FP32 parameters (own included,
+        # through the switch); out: all bf16 gradients + the FP32 piece once
+        nvl_bytes = max(2 * P // world + 4 * P, 2 * P + 4 * P // world)
+    else:
+        nvl_bytes = 6 * P * (world - 1) // world  # bf16 RS + FP32 AG, per direction
     peak, peak_kind = measured_hbm_peak()
     t_hbm = hbm_bytes / (peak * 1e9)
     t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
@@ -518,8 +523,9 @@ def run_sharded(args, rank, world, device):
                             "parameter vector: bf16 error-feedback compression, reduce of "
                             "the bf16 gradients, packed-moment step on the rank's 1/N, FP32 "
                             "parameter broadcast (peer: one fused kernel over NVLink peer "
-                            "memory between two barriers; nccl: reduce-scatter + step + "
-                            "all-gather)",
+                            "memory between two barriers; nvls: the same kernel reducing and "
+                            "broadcasting through NVSwitch multicast; nccl: reduce-scatter + "
+                            "step + all-gather)",
                 "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
                 "transport": opt.transport,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
@@ -530,7 +536,7 @@ def run_sharded(args, rank, world, device):
                          "hbm_bytes_per_rank": hbm_bytes, "nvlink_bytes_per_rank": nvl_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": f"{peak_kind} hbm_gbs",
                          "nvlink_gbs": NVLINK_GBS, "traffic": None},
-            "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport == "peer"
+            "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport in ("peer", "nvls")
                                  else 2 * opt.n_buckets),
             "clocks": clocks,
         }

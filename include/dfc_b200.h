@@ -249,14 +249,29 @@ DFC_API int dfc_fiber_write(const DfcWordRange* ranges, int32_t n_ranges, int64_
  * mapped into this process (symmetric memory); 16-byte aligned.  For every
  * element j of the segments: g = comp_0[j] + comp_1[j] + ... (FP32, rank
  * order), the DFC-AdamW step on this rank's moment words, then the new
- * parameter stored to param_q[j] of every rank q.  The caller brackets the
- * call with dfc_peer_barrier: before it so every rank's gradients are
- * complete, after it so every rank's parameters are.
+ * parameter stored to param_q[j] of every rank q.
+ * comp_multicast, param_multicast: NULL, or the NVLink-multicast (NVSwitch)
+ * addresses of the same two buffers; then the switch does the reduction
+ * (multimem.ld_reduce, FP32 accumulation, result rounded to bf16 by the
+ * switch) and the broadcast (multimem.st), for every element;
+ * dfc_multicast_sum_bf16 returns the g values the switch produces.
+ * The caller brackets the call with dfc_peer_barrier: before it so every
+ * rank's gradients are complete, after it so every rank's parameters are.
  */
 DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
+                                const void* comp_multicast, void* param_multicast,
                                 int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                 int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                 int32_t mode, const float* device_grad_scale, void* stream);
+
+/*
+ * The NVSwitch sum over every rank of numel bf16 values at a multicast
+ * address, written as FP32 to out (device, 16-byte aligned): exactly the
+ * gradient values the multicast form of dfc_zero_fused_step steps with.  No
+ * reference counterpart; for checking the reduction.
+ */
+DFC_API int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64_t numel,
+                                   void* stream);
 
 /*
  * Barrier across ranks on their streams.  slot_ptrs: host array of n_peers

@@ -66,7 +66,7 @@ EXPORTS = (
     "dfc_pack_moments", "dfc_unpack_moments", "dfc_compress_ef",
     "dfc_grad_stats_scratch_bytes", "dfc_grad_stats", "dfc_clip_coef",
     "dfc_fiber_read", "dfc_fiber_write", "dfc_grad_stats_noalloc",
-    "dfc_zero_fused_step", "dfc_peer_barrier",
+    "dfc_zero_fused_step", "dfc_peer_barrier", "dfc_multicast_sum_bf16",
 )
 
 
@@ -100,8 +100,9 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_fiber_read": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_fiber_write": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
-        "dfc_zero_fused_step": ([P, P, I32, I32, P, I32, P, I32, I32, P, P], ctypes.c_int),
+        "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P], ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
+        "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(h, name)

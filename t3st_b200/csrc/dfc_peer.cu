@@ -12,7 +12,13 @@
 // once (4 B per element per peer), the reduction happens in registers in
 // FP32 (deterministic order, no bf16 re-rounding of partial sums), and no
 // reduce-scatter output buffer or all-gather staging is written to HBM.  Only
-// plain loads and stores touch peer memory (no TMA, no multicast).
+// plain loads and stores touch peer memory (no TMA).
+//
+// NVLS form (multicast addresses given): the NVSwitch does the reduction
+// (multimem.ld_reduce, FP32 accumulation, bf16 result) and replicates the
+// parameter stores (multimem.st), so each value crosses this GPU's links
+// once instead of once per peer.  dfc_multicast_sum_bf16 reads the switch's
+// sums back, for checking.
 //
 // dfc_peer_barrier orders the ranks around it: each rank writes an epoch to
 // its slot in every peer's signal array (release, system scope) and then
@@ -45,6 +51,8 @@ template <int MAXS, int MAXH>
 struct ZeroBatch {
   const uint16_t* comp[kMaxPeers];  // every rank's compressed gradients (bf16 bits)
   float* param[kMaxPeers];          // every rank's flat FP32 parameters
+  const uint16_t* comp_mc;          // multicast address of the gradients (nvls kernel)
+  float* param_mc;                  // multicast address of the parameters (nvls kernel)
   const float* dev_scale;
   int32_t n_peers;
   int32_t rank;
@@ -119,21 +127,98 @@ __device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerS
   }
 }
 
+// The switch's sum of element j over every rank: the aligned bf16x2 word
+// that holds j is reduced (FP32 accumulation, bf16 result) and j's half kept.
+// The word never leaves the 4-byte granule of a valid element.
+__device__ __forceinline__ float nvls_sum1(const uint16_t* mc, int64_t j) {
+  uint32_t w;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.bf16x2 %0, [%1];"
+               : "=r"(w)
+               : "l"(mc + (j & ~int64_t(1)))
+               : "memory");
+  return u2f((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
+}
+
+__device__ __forceinline__ void nvls_sum8(const uint16_t* mc, float (&g)[8]) {
+  uint32_t r[4];
+  asm volatile(
+      "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "l"(mc)
+      : "memory");
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    g[2 * k] = u2f(r[k] << 16);
+    g[2 * k + 1] = u2f(r[k] & 0xFFFF0000u);
+  }
+}
+
+// NVLS (NVSwitch multicast): the switch sums the 8 bf16 values at comp_mc + j
+// of every rank with FP32 accumulation and returns them rounded to bf16; one
+// multicast store writes the new parameters into every rank's copy.  Each
+// value crosses this GPU's links once instead of once per peer.
 template <int MODE, int MAXS, int MAXH>
+__device__ __forceinline__ void vec8_nvls(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
+                                          int64_t local, const Scalars& s) {
+  const int64_t j = sg.offset + local;
+  float g[8];
+  nvls_sum8(b.comp_mc + j, g);
+  const float* mine = b.param[b.rank] + j;
+  float4 p0 = __ldcs(reinterpret_cast<const float4*>(mine));
+  float4 p1 = __ldcs(reinterpret_cast<const float4*>(mine + 4));
+  uint4 m0 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local));
+  uint4 m1 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local + 4));
+  uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local));
+  uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local + 4));
+  step_elem<MODE>(s, p0.x, g[0], m0.x, v0.x);
+  step_elem<MODE>(s, p0.y, g[1], m0.y, v0.y);
+  step_elem<MODE>(s, p0.z, g[2], m0.z, v0.z);
+  step_elem<MODE>(s, p0.w, g[3], m0.w, v0.w);
+  step_elem<MODE>(s, p1.x, g[4], m1.x, v1.x);
+  step_elem<MODE>(s, p1.y, g[5], m1.y, v1.y);
+  step_elem<MODE>(s, p1.z, g[6], m1.z, v1.z);
+  step_elem<MODE>(s, p1.w, g[7], m1.w, v1.w);
+  __stcs(reinterpret_cast<uint4*>(sg.m + local), m0);
+  __stcs(reinterpret_cast<uint4*>(sg.m + local + 4), m1);
+  __stcs(reinterpret_cast<uint4*>(sg.v + local), v0);
+  __stcs(reinterpret_cast<uint4*>(sg.v + local + 4), v1);
+  float* dst = b.param_mc + j;
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+               "f"(p0.x), "f"(p0.y), "f"(p0.z), "f"(p0.w)
+               : "memory");
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4),
+               "f"(p1.x), "f"(p1.y), "f"(p1.z), "f"(p1.w)
+               : "memory");
+}
+
+// One element.  Plain form: peer loads, FP32 sum in rank order, peer stores.
+// NVLS form: the switch's sum and one multicast store, as in vec8_nvls, so
+// every element of a bucket follows the switch's rounding.
+template <int MODE, bool NVLS, int MAXS, int MAXH>
 __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
                                         int64_t local, const Scalars& s) {
   const int64_t j = sg.offset + local;
-  float g = bf16_bits_to_f32(b.comp[0][j]);
-  for (int q = 1; q < b.n_peers; ++q) g = __fadd_rn(g, bf16_bits_to_f32(b.comp[q][j]));
+  float g;
+  if (NVLS) {
+    g = nvls_sum1(b.comp_mc, j);
+  } else {
+    g = bf16_bits_to_f32(b.comp[0][j]);
+    for (int q = 1; q < b.n_peers; ++q) g = __fadd_rn(g, bf16_bits_to_f32(b.comp[q][j]));
+  }
   float p = b.param[b.rank][j];
   uint32_t m = sg.m[local], v = sg.v[local];
   step_elem<MODE>(s, p, g, m, v);
   sg.m[local] = m;
   sg.v[local] = v;
-  for (int q = 0; q < b.n_peers; ++q) b.param[q][j] = p;
+  if (NVLS) {
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(b.param_mc + j), "f"(p)
+                 : "memory");
+  } else {
+    for (int q = 0; q < b.n_peers; ++q) b.param[q][j] = p;
+  }
 }
 
-template <int MODE, int NP, int MAXS, int MAXH>
+template <int MODE, int NP, bool NVLS, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
   const int32_t t = static_cast<int32_t>(blockIdx.x);
@@ -149,19 +234,27 @@ __global__ void __launch_bounds__(kThreads)
   int64_t done = 0;
   if (sg.vec) {
     const int64_t nv = count / kVec;
-    for (int64_t k = threadIdx.x; k < nv; k += kThreads) vec8<MODE, NP>(b, sg, base + k * kVec, s);
+    for (int64_t k = threadIdx.x; k < nv; k += kThreads) {
+      if (NVLS) vec8_nvls<MODE>(b, sg, base + k * kVec, s);
+      else vec8<MODE, NP>(b, sg, base + k * kVec, s);
+    }
     done = nv * kVec;
   }
-  for (int64_t k = done + threadIdx.x; k < count; k += kThreads) scalar1<MODE>(b, sg, base + k, s);
+  for (int64_t k = done + threadIdx.x; k < count; k += kThreads)
+    scalar1<MODE, NVLS>(b, sg, base + k, s);
 }
 
 template <int MODE, int MAXS, int MAXH>
 void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t tiles, cudaStream_t st) {
+  if (b.comp_mc) {
+    zero_step_kernel<MODE, 0, true><<<tiles, kThreads, 0, st>>>(b);
+    return;
+  }
   switch (b.n_peers) {
-    case 2: zero_step_kernel<MODE, 2><<<tiles, kThreads, 0, st>>>(b); break;
-    case 4: zero_step_kernel<MODE, 4><<<tiles, kThreads, 0, st>>>(b); break;
-    case 8: zero_step_kernel<MODE, 8><<<tiles, kThreads, 0, st>>>(b); break;
-    default: zero_step_kernel<MODE, 0><<<tiles, kThreads, 0, st>>>(b); break;
+    case 2: zero_step_kernel<MODE, 2, false><<<tiles, kThreads, 0, st>>>(b); break;
+    case 4: zero_step_kernel<MODE, 4, false><<<tiles, kThreads, 0, st>>>(b); break;
+    case 8: zero_step_kernel<MODE, 8, false><<<tiles, kThreads, 0, st>>>(b); break;
+    default: zero_step_kernel<MODE, 0, false><<<tiles, kThreads, 0, st>>>(b); break;
   }
 }
 
@@ -175,6 +268,23 @@ int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
     default: launch_np<DFC_MODE_PACKED>(b, tiles, st); break;
   }
   return launch_status();
+}
+
+// ---- the switch's sums, read back ----------------------------------------
+__global__ void __launch_bounds__(kThreads)
+    multicast_sum_kernel(const uint16_t* mc, float* out, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  const int64_t n8 = n / kVec;
+  for (int64_t k = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; k < n8; k += stride) {
+    float g[8];
+    nvls_sum8(mc + k * kVec, g);
+    float4* o = reinterpret_cast<float4*>(out + k * kVec);
+    o[0] = make_float4(g[0], g[1], g[2], g[3]);
+    o[1] = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  for (int64_t j = n8 * kVec + blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; j < n;
+       j += stride)
+    out[j] = nvls_sum1(mc, j);
 }
 
 // ---- barrier --------------------------------------------------------------
@@ -229,6 +339,7 @@ bool peers_ok(const void* const* ptrs, int32_t n) {
 }  // namespace dfc
 
 extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
+                                   const void* comp_multicast, void* param_multicast,
                                    int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                    int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                    int32_t mode, const float* device_grad_scale, void* stream) {
@@ -242,6 +353,8 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
   if (!peers_ok(comp_ptrs, n_peers) || !peers_ok(param_ptrs, n_peers)) return DFC_ERR_NULL;
   for (int32_t q = 0; q < n_peers; ++q)
     if (!aligned(comp_ptrs[q], 16) || !aligned(param_ptrs[q], 16)) return DFC_ERR_ALIGN;
+  if ((comp_multicast == nullptr) != (param_multicast == nullptr)) return DFC_ERR_NULL;
+  if (!aligned(comp_multicast, 16) || !aligned(param_multicast, 16)) return DFC_ERR_ALIGN;
   for (int32_t i = 0; i < n_segments; ++i) {
     const DfcPeerSegment& s = segments[i];
     if (s.numel < 0 || s.offset < 0) return DFC_ERR_SIZE;
@@ -256,6 +369,8 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     b.comp[q] = q < n_peers ? static_cast<const uint16_t*>(comp_ptrs[q]) : nullptr;
     b.param[q] = q < n_peers ? static_cast<float*>(param_ptrs[q]) : nullptr;
   }
+  b.comp_mc = static_cast<const uint16_t*>(comp_multicast);
+  b.param_mc = static_cast<float*>(param_multicast);
   b.dev_scale = device_grad_scale;
   b.n_peers = n_peers;
   b.rank = rank;
@@ -296,6 +411,19 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     ++b.n_segs;
   }
   return b.n_segs ? launch(b, mode, st) : DFC_OK;
+}
+
+extern "C" int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64_t numel,
+                                      void* stream) {
+  using namespace dfc;
+  if (numel < 0) return DFC_ERR_SIZE;
+  if (numel == 0) return DFC_OK;
+  if (!comp_multicast || !out) return DFC_ERR_NULL;
+  if (!aligned(comp_multicast, 16) || !aligned(out, 16)) return DFC_ERR_ALIGN;
+  const int64_t blocks = std::min<int64_t>((numel / kVec + kThreads - 1) / kThreads + 1, 148 * 8);
+  multicast_sum_kernel<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(comp_multicast), out, numel);
+  return launch_status();
 }
 
 extern "C" int dfc_peer_barrier(uint32_t* const* slot_ptrs, int32_t n_peers, int32_t rank,

@@ -116,18 +116,18 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.compress = (self.world > 1) if compress_grads is None else bool(compress_grads)
         self.average = bool(average_grads)
         self.kernels = backend if backend is not None else CudaKernels()
-        if transport not in ("auto", "nccl", "peer"):
-            raise ValueError("transport must be 'auto', 'nccl' or 'peer'")
+        if transport not in ("auto", "nccl", "peer", "nvls"):
+            raise ValueError("transport must be 'auto', 'nccl', 'peer' or 'nvls'")
         if transport == "auto":
             on_cuda = all(p.is_cuda for g in self.param_groups for p in g["params"])
             fused_ok = self.world == 2 and self.compress and backend is None and on_cuda
             transport = "peer" if fused_ok else "nccl"
         self.transport = transport if self.world > 1 else "nccl"
-        if self.transport == "peer" and not self.compress:
-            raise ValueError("the peer transport reduces bf16 compressed gradients")
+        if self.transport in ("peer", "nvls") and not self.compress:
+            raise ValueError("the peer and nvls transports reduce bf16 compressed gradients")
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
         self._layout(bucket_elems)
-        if self.transport == "peer":
+        if self.transport in ("peer", "nvls"):
             self._setup_peer()
 
     # ---- layout -----------------------------------------------------------
@@ -198,7 +198,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
 
     def _alloc(self, n: int, dtype) -> torch.Tensor:
         """Zeroed buffer; in symmetric (peer-mapped) memory for the peer transport."""
-        if self.transport == "peer":
+        if self.transport in ("peer", "nvls"):
             import torch.distributed._symmetric_memory as symm_mem
 
             t = symm_mem.empty(n, dtype=dtype, device=self.device)
@@ -226,12 +226,21 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             if len(ptrs) != n or off < 0 or off + nbytes > int(h.buffer_size) or \
                     (hasattr(h, "offset") and int(h.offset) != off):
                 raise RuntimeError("symmetric-memory layout is not the expected one")
-            return [p + off for p in ptrs], h
+            mc = None
+            if self.transport == "nvls":
+                from torch._C._distributed_c10d import _SymmetricMemory
+
+                if not _SymmetricMemory.has_multicast_support(
+                        torch._C._autograd.DeviceType.CUDA, self.device.index) or \
+                        not int(h.multicast_ptr):
+                    raise RuntimeError("NVLink multicast is not available on this node")
+                mc = int(h.multicast_ptr) + off
+            return [p + off for p in ptrs], h, mc
 
         self.slots = symm_mem.empty(n, dtype=torch.int32, device=self.device).zero_()
-        self._param_peers, self._h_param = peers(self.flat_param)
-        self._comp_peers, self._h_comp = peers(self.comp)
-        self._slot_peers, self._h_slots = peers(self.slots)
+        self._param_peers, self._h_param, self._param_mc = peers(self.flat_param)
+        self._comp_peers, self._h_comp, self._comp_mc = peers(self.comp)
+        self._slot_peers, self._h_slots, _ = peers(self.slots)
         self.peer_error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._epoch = 0
         torch.cuda.synchronize(self.device)
@@ -274,15 +283,15 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 if len(segs):
                     segs["hyper"] = index[b]
                     _lib.check("dfc_zero_fused_step", lib.dfc_zero_fused_step(
-                        _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self.world,
-                        self.rank, _lib.ptr(segs), len(segs), _lib.ptr(hyp), len(rows),
-                        self.mode, None, side.cuda_stream))
+                        _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self._comp_mc,
+                        self._param_mc, self.world, self.rank, _lib.ptr(segs), len(segs),
+                        _lib.ptr(hyp), len(rows), self.mode, None, side.cuda_stream))
             self._barrier(side.cuda_stream)
         main.wait_stream(side)
 
     def peer_status(self) -> int:
         """0, or 1 + the rank a barrier gave up waiting for (synchronises)."""
-        return int(self.peer_error.item()) if self.transport == "peer" else 0
+        return int(self.peer_error.item()) if self.transport in ("peer", "nvls") else 0
 
     def _bucket(self, t: torch.Tensor, b: int) -> torch.Tensor:
         return t[b * self.bucket:(b + 1) * self.bucket]
@@ -352,7 +361,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 idx.append(j)
             index.append(idx)
 
-        if self.transport == "peer":
+        if self.transport in ("peer", "nvls"):
             self._step_peer(rows, index)
             return loss
 
@@ -402,6 +411,16 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     def full_reduced_grad(self) -> torch.Tensor:
         """The gradient the last step used, in flat order on every rank
         (collective; for checking and debugging)."""
+        if self.transport == "nvls":
+            # the switch's sums, read through the multicast address; the barrier
+            # keeps every rank's gradients in place until all have read them
+            out = torch.empty(self.padded, dtype=torch.float32, device=self.device)
+            _lib.check("dfc_multicast_sum_bf16", _lib.lib().dfc_multicast_sum_bf16(
+                self._comp_mc, out.data_ptr(), self.padded,
+                torch.cuda.current_stream(self.device).cuda_stream))
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            return out
         if self.transport == "peer":
             # the fused kernel sums every rank's bf16 values in FP32, rank order
             allc = torch.empty(self.world * self.padded, dtype=torch.bfloat16, device=self.device)

@@ -1,7 +1,7 @@
 """ZeRO-1 ShardedDFCAdamW on CUDA: one GPU (no collective), and two GPUs
-over NCCL when the machine has them (the bf16 reduce-scatter result is read
-back from every shard and the step is checked bit for bit against the oracle
-given that reduced gradient)."""
+over NCCL, NVLink peer memory or NVSwitch multicast when the machine has
+them (the reduced gradient is read back from every shard and the step is
+checked bit for bit against the oracle given that reduced gradient)."""
 
 import os
 import socket
@@ -21,6 +21,28 @@ SHAPES = [(257, 31), (31,), (4099,), (3, 3, 3), (1 << 16,)]
 def _grads(rank, step, sizes):
     rng = np.random.default_rng(1000 * step + rank)
     return [(rng.standard_normal(n) * 1e-3).astype(np.float32) for n in sizes]
+
+
+def _bf16_bracket(x):
+    """The two bf16 values next to each float64 x (equal when x is one)."""
+    _, e = np.frexp(x)
+    ulp = np.ldexp(1.0, np.maximum(e, -125) - 8)
+    lo = np.floor(x / ulp) * ulp
+    return lo, np.where(lo == x, lo, lo + ulp)
+
+
+def _check_switch_sums(opt, red, world):
+    """The switch's sums are a faithful bf16 rounding of the exact sum of
+    every rank's bf16 values (the neighbour below or above it)."""
+    import torch.distributed as dist
+
+    allc = torch.empty(world * opt.padded, dtype=torch.bfloat16, device=opt.device)
+    dist.all_gather_into_tensor(allc, opt.comp.view(torch.bfloat16))
+    exact = allc.view(world, opt.padded).double().sum(0).cpu().numpy()
+    lo, hi = _bf16_bracket(exact)
+    got = red.double().cpu().numpy()
+    bad = np.flatnonzero((got != lo) & (got != hi))
+    assert bad.size == 0, (bad[:8], got[bad[:8]], exact[bad[:8]])
 
 
 def _run(rank, world, device, compress, transport="nccl"):
@@ -45,9 +67,11 @@ def _run(rank, world, device, compress, transport="nccl"):
         torch.cuda.synchronize()
         if world > 1:
             red = opt.full_reduced_grad()
+            if transport == "nvls":
+                _check_switch_sums(opt, red, world)
             if red.dtype == torch.bfloat16:  # NCCL's bf16 sum
                 red = red.view(torch.int16).cpu().numpy().view(np.uint16)
-            else:                            # the fused kernel's FP32 sum, rank order
+            else:  # the fused kernel's FP32 sum in rank order (nvls: rounded to bf16)
                 red = red.cpu().numpy()
             gsrc = [red[off:off + n].copy() for off, n in zip(opt.offsets, sizes)]
             scale = 1.0 / world
@@ -118,10 +142,19 @@ def _worker(rank, world, port, transport, q):
         q.put((rank, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("transport", ["nccl", "peer"])
+def _multicast_ok() -> bool:
+    from torch._C._autograd import DeviceType
+    from torch._C._distributed_c10d import _SymmetricMemory
+
+    return _SymmetricMemory.has_multicast_support(DeviceType.CUDA, 0)
+
+
+@pytest.mark.parametrize("transport", ["nccl", "peer", "nvls"])
 def test_sharded_on_two_gpus(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    if transport == "nvls" and not _multicast_ok():
+        pytest.skip("no NVLink multicast on this node")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
