@@ -58,6 +58,8 @@ def parse_args():
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-clocks", action="store_true",
                     help="skip the nvidia-smi clock sampler (profiling runs)")
+    ap.add_argument("--no-replay", action="store_true",
+                    help="skip the replay-record codec measurement")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
     ap.add_argument("--transport", choices=("auto", "peer", "nvls", "nccl"), default="auto",
@@ -398,7 +400,77 @@ def run_single(args, device):
         rate, desc, cores = cpu_port_rate(resnet18_cifar_shapes(), args.cpu_seconds, packed=True)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": desc}
+    if not args.no_replay:
+        line["replay"] = run_replay(device, peak, peak_kind, cpu=not args.no_cpu_baseline)
     return line
+
+
+REPLAY_BATCH = 65536                   # records per launch (805 MB of FP32 images)
+REPLAY_ENCODE_BYTES = 3072 * 4 + 8 + 1552   # image + label + task in, record out
+REPLAY_DECODE_BYTES = 1552 + 3072 * 4 + 12  # record in, image + label + task + status out
+
+
+def run_replay(device, peak, peak_kind, cpu=True, reps=10):
+    """The replay-record codec (dfc_replay_encode / dfc_replay_decode) on a
+    batch of 65,536 records, each launch timed with CUDA events on the
+    launching stream; beside it the CPU codec (the oracle's restatement of
+    the reference's per-record numpy + zlib codec, one thread)."""
+    from oracle import replay as R
+    from t3st_b200 import _lib
+
+    n = REPLAY_BATCH
+    g = torch.Generator(device=device).manual_seed(3)
+    x = torch.rand((n, 3072), generator=g, device=device)
+    y = torch.randint(0, 100, (n,), generator=g, device=device, dtype=torch.int32)
+    t = torch.randint(0, 10, (n,), generator=g, device=device, dtype=torch.int32)
+    rec = torch.empty((n, 1552), dtype=torch.uint8, device=device)
+    out = torch.empty((n, 3072), device=device)
+    meta = torch.empty((3, n), dtype=torch.int32, device=device)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(device)
+
+    def enc():
+        _lib.check("dfc_replay_encode", lib.dfc_replay_encode(
+            x.data_ptr(), 3072, y.data_ptr(), t.data_ptr(), n, rec.data_ptr(), 1552,
+            stream.cuda_stream))
+
+    def dec():
+        _lib.check("dfc_replay_decode", lib.dfc_replay_decode(
+            rec.data_ptr(), 1552, n, out.data_ptr(), meta[0].data_ptr(), meta[1].data_ptr(),
+            meta[2].data_ptr(), stream.cuda_stream))
+
+    res = {"batch_records": n, "launches_timed": 2 * reps,
+           "l2": "805 MB of images per launch > 126 MB L2 (no flush)"}
+    for name, fn, nbytes in (("encode", enc, REPLAY_ENCODE_BYTES), ("decode", dec, REPLAY_DECODE_BYTES)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sec = e0.elapsed_time(e1) / 1e3 / reps
+        gbs = n * nbytes / sec / 1e9
+        res[name] = {"records_per_s": n / sec, "us_per_launch": sec * 1e6,
+                     "algorithmic_bytes_per_record": nbytes,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                  "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs"}}
+    if int(meta[2].abs().sum()) != 0:
+        raise RuntimeError("replay bench: a record failed its CRC check")
+    if cpu:
+        xs, ys, ts = x[:2000].cpu().numpy(), y[:2000].cpu().numpy(), t[:2000].cpu().numpy()
+        t0 = time.perf_counter()
+        k = 0
+        while k < len(xs) and (time.perf_counter() - t0 < 2.0 or k < 100):
+            R.decode(R.encode(xs[k], int(ys[k]), int(ts[k])))
+            k += 1
+        el = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": k / el, "unit": "records/s (encode + decode)", "cores": 1,
+                               "kind": "port",
+                               "sample": f"{k} records through the numpy + zlib codec"}
+    return res
 
 
 def run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K):

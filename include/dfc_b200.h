@@ -125,6 +125,13 @@ typedef struct DfcGradStats {
   int64_t nonfinite;   /* number of Inf/NaN elements */
 } DfcGradStats;
 
+/* Replay records (remote/vision_benchmark.py:74-100, CIFAR4BitCodec). */
+#define DFC_REPLAY_RECORD_BYTES 1552
+#define DFC_REPLAY_PIXELS 3072
+#define DFC_RECORD_OK 0          /* magic and CRC-32 match */
+#define DFC_RECORD_BAD_MAGIC 1   /* first four bytes are not "CF4B" */
+#define DFC_RECORD_BAD_CRC 2     /* stored CRC-32 differs from the computed one */
+
 /* Most ranks a fused ZeRO-1 call can span. */
 #define DFC_MAX_PEERS 8
 
@@ -239,6 +246,30 @@ DFC_API int dfc_fiber_read(const DfcWordRange* ranges, int32_t n_ranges, int64_t
                    int64_t n_bits, uint8_t* bytes, void* stream);
 DFC_API int dfc_fiber_write(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
                     int64_t n_bits, const uint8_t* bytes, void* stream);
+
+/*
+ * Replay-record codec on the device, one warp per record (replaces the
+ * per-record host codec CIFAR4BitCodec.encode / .decode,
+ * remote/vision_benchmark.py:79-100).  Record layout: "CF4B", label and task
+ * as uint16 little-endian, 3072 pixels quantised to 4 bits as
+ * clamp(round_half_even(x * 15), 0, 15) (NaN -> 0), two per byte with the
+ * even pixel in the low nibble, the zlib CRC-32 of bytes [0, 1544)
+ * little-endian, four zero bytes.
+ *
+ * dfc_replay_encode: images (device FP32, 16-byte aligned, image_stride
+ * floats between records, a multiple of 4 and >= 3072), labels and tasks
+ * (device int32; the low 16 bits are stored) -> records (device, 16-byte
+ * aligned, record_stride bytes apart, a multiple of 16 and >= 1552).
+ * dfc_replay_decode: records -> images (device FP32, contiguous, q / 15),
+ * labels, tasks and status (device int32, DFC_RECORD_*).  Every record is
+ * decoded whatever its status; the caller checks status.
+ */
+DFC_API int dfc_replay_encode(const float* images, int64_t image_stride, const int32_t* labels,
+                              const int32_t* tasks, int64_t n_records, uint8_t* records,
+                              int64_t record_stride, void* stream);
+DFC_API int dfc_replay_decode(const uint8_t* records, int64_t record_stride, int64_t n_records,
+                              float* images, int32_t* labels, int32_t* tasks, int32_t* status,
+                              void* stream);
 
 /*
  * ZeRO-1 shard step fused with its collectives over NVLink peer memory (no

@@ -32,6 +32,11 @@ DFC_ERR_SCRATCH = -9
 # partial records available to dfc_grad_stats_noalloc (include/dfc_b200.h)
 GRAD_STATS_STATIC_RECORDS = 65536
 
+# replay records (include/dfc_b200.h)
+REPLAY_RECORD_BYTES = 1552
+REPLAY_PIXELS = 3072
+RECORD_OK, RECORD_BAD_MAGIC, RECORD_BAD_CRC = 0, 1, 2
+
 MODE_PLAIN = 0
 MODE_SIGNFIBER = 1
 MODE_PACKED = 2
@@ -67,6 +72,7 @@ EXPORTS = (
     "dfc_grad_stats_scratch_bytes", "dfc_grad_stats", "dfc_clip_coef",
     "dfc_fiber_read", "dfc_fiber_write", "dfc_grad_stats_noalloc",
     "dfc_zero_fused_step", "dfc_peer_barrier", "dfc_multicast_sum_bf16",
+    "dfc_replay_encode", "dfc_replay_decode",
 )
 
 
@@ -103,6 +109,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P], ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
         "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
+        "dfc_replay_encode": ([P, I64, P, P, I64, P, I64, P], ctypes.c_int),
+        "dfc_replay_decode": ([P, I64, I64, P, P, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(h, name)

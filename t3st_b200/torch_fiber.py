@@ -422,25 +422,33 @@ class TorchSignFiberChannel:
         if start < 0 or count < 0 or start + count > self.bit_capacity:
             raise IndexError("fiber range out of bounds")
 
+    def _read_dev(self, start: int, count: int) -> torch.Tensor:
+        out = torch.empty((count + 7) // 8, dtype=torch.uint8, device=self.device)
+        if count:
+            with torch.cuda.device(self.device):
+                _lib.check("dfc_fiber_read", _lib.lib().dfc_fiber_read(
+                    _lib.ptr(self._ranges), len(self._ranges), start, count, out.data_ptr(),
+                    torch.cuda.current_stream(self.device).cuda_stream))
+        return out
+
+    def _write_dev(self, start: int, count: int, src: torch.Tensor) -> None:
+        if count == 0:
+            return
+        with torch.cuda.device(self.device):
+            src = src.to(device=self.device, dtype=torch.uint8).contiguous()
+            _lib.check("dfc_fiber_write", _lib.lib().dfc_fiber_write(
+                _lib.ptr(self._ranges), len(self._ranges), start, count, src.data_ptr(),
+                torch.cuda.current_stream(self.device).cuda_stream))
+
     def _read_packed(self, start: int, count: int) -> np.ndarray:
-        nbytes = (count + 7) // 8
         if count == 0:
             return np.empty(0, dtype=np.uint8)
-        with torch.cuda.device(self.device):
-            out = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
-            _lib.check("dfc_fiber_read", _lib.lib().dfc_fiber_read(
-                _lib.ptr(self._ranges), len(self._ranges), start, count, out.data_ptr(),
-                torch.cuda.current_stream(self.device).cuda_stream))
-            return out.cpu().numpy()
+        return self._read_dev(start, count).cpu().numpy()
 
     def _write_packed(self, start: int, count: int, packed: np.ndarray) -> None:
         if count == 0:
             return
-        with torch.cuda.device(self.device):
-            src = torch.from_numpy(np.array(packed, dtype=np.uint8, copy=True)).to(self.device)
-            _lib.check("dfc_fiber_write", _lib.lib().dfc_fiber_write(
-                _lib.ptr(self._ranges), len(self._ranges), start, count, src.data_ptr(),
-                torch.cuda.current_stream(self.device).cuda_stream))
+        self._write_dev(start, count, torch.from_numpy(np.array(packed, dtype=np.uint8, copy=True)))
 
     @torch.no_grad()
     def read_bits(self, start: int, count: int) -> np.ndarray:
@@ -466,6 +474,25 @@ class TorchSignFiberChannel:
         if start < 0 or start + len(raw) > self.byte_capacity:
             raise IndexError("fiber byte range out of bounds")
         self._write_packed(int(start) * 8, len(raw) * 8, np.frombuffer(raw, dtype=np.uint8))
+
+    # device-resident byte I/O (no reference counterpart): the replay codec
+    # moves records between the fiber and its kernels without a host copy
+    @torch.no_grad()
+    def read_device(self, start: int, count: int) -> torch.Tensor:
+        """Bytes [start, start + count) as a uint8 tensor on the fiber's device."""
+        if start < 0 or count < 0 or start + count > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        return self._read_dev(int(start) * 8, int(count) * 8)
+
+    @torch.no_grad()
+    def write_device(self, start: int, data: torch.Tensor) -> None:
+        """Write the uint8 tensor ``data`` (any device) at byte ``start``."""
+        if data.dtype != torch.uint8:
+            raise TypeError("fiber bytes are uint8")
+        n = data.numel()
+        if start < 0 or start + n > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        self._write_dev(int(start) * 8, n * 8, data.reshape(-1))
 
 
 def local_fiber_capacity(optimizer: DFCAdamW) -> dict[str, int]:

@@ -32,6 +32,13 @@ Cases (all FP32):
   bf16_params,   3 bf16 (or fp16) parameter tensors (1031, 300, 7) with
   f16_params     gradients of the same type, 6 steps, payload, lr 1e-3, wd 0.01;
                  p is stored as the 16-bit patterns.
+  replay         the replay codec and reservoir of remote/vision_benchmark.py
+                 (:74-151): 24 seeded images (on the 1/255 grid like ToTensor,
+                 plus exact quantisation ties, values outside [0, 1], -0.0,
+                 +-Inf and NaN), their records from CIFAR4BitCodec.encode,
+                 the decoded images, corrupted records with the error each
+                 raises, and a FiberReservoir over an ArrayChannel (room for
+                 5 records) after 12 adds and a sample of 6 (seeded rng).
   unit_linear    the reference's own unit-test trajectory
                  (remote/test_torch_fiber.py:11-31): Linear(257,31), seed 17,
                  50 steps of MSE, lr 3e-4, wd 0.01; final params of the
@@ -276,9 +283,64 @@ def case_unit_linear(tf):
          w=reference.weight.detach().numpy(), b=reference.bias.detach().numpy())
 
 
+def replay_images(n=24, seed=5):
+    rng = np.random.default_rng(seed)
+    x = (rng.integers(0, 256, (n, 3, 32, 32)) / 255.0).astype(np.float32)
+    flat = x.reshape(n, -1)
+    # exact ties k + 0.5 after the FP32 multiply by 15, both parities
+    ties = np.array([(k + 0.5) / 15.0 for k in range(15)], np.float32)
+    flat[1, :15] = ties
+    flat[2, :64] = rng.uniform(-0.5, 1.5, 64).astype(np.float32)
+    flat[3, :6] = np.array([-0.0, np.inf, -np.inf, np.nan, 1.0, 0.0], np.float32)
+    flat[4] = np.float32(1.0)
+    flat[5] = np.float32(0.0)
+    labels = rng.integers(0, 100, n)
+    tasks = labels // 10
+    labels[6], tasks[6] = 65535, 65535
+    return x, labels, tasks
+
+
+def case_replay(vb):
+    x, labels, tasks = replay_images()
+    codec = vb.CIFAR4BitCodec
+    records = np.stack([np.frombuffer(codec.encode(torch.from_numpy(x[i]), int(labels[i]),
+                                                   int(tasks[i])), np.uint8)
+                        for i in range(len(x))])
+    dec = [codec.decode(r.tobytes()) for r in records]
+    decoded = np.stack([d[0].numpy().reshape(-1) for d in dec])
+    # corruptions: a flipped pixel bit, a flipped CRC bit, a bad magic, a
+    # flipped header bit; the error text each raises
+    bad = records[:4].copy()
+    bad[0, 100] ^= 0x10
+    bad[1, 1545] ^= 0x01
+    bad[2, 0] = ord("X")
+    bad[3, 5] ^= 0x80
+    errors = []
+    for r in bad:
+        try:
+            codec.decode(r.tobytes())
+            errors.append("")
+        except RuntimeError as e:
+            errors.append(str(e))
+    # reservoir: ArrayChannel with room for 5 records and 100 spare bytes
+    channel = vb.ArrayChannel(vb.FiberReservoir.HEADER_BYTES + 5 * codec.RECORD_BYTES + 100)
+    res = vb.FiberReservoir(channel)
+    rng = np.random.default_rng(11)
+    for i in range(12):
+        res.add(torch.from_numpy(x[i]), int(labels[i]), int(tasks[i]), rng)
+    channel_after_adds = np.frombuffer(bytes(channel.storage), np.uint8).copy()
+    sx, sy = res.sample(6, rng)
+    save("replay", images=x, labels=labels, tasks=tasks, records=records, decoded=decoded,
+         dec_labels=np.array([d[1] for d in dec]), dec_tasks=np.array([d[2] for d in dec]),
+         bad_records=bad, bad_errors=np.array(errors), res_capacity=res.capacity,
+         res_size=res.size, res_seen=res.seen, res_rng_seed=11, res_adds=12,
+         channel=channel_after_adds, sample_x=sx.numpy(), sample_y=sy.numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default=None, help="make one case (by file name)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "remote"))
     sys.path.insert(0, REPO)
@@ -286,6 +348,11 @@ def main():
     from oracle import oracle
 
     torch.set_num_threads(1)
+    if args.only == "replay":
+        import vision_benchmark as vb  # the reference's benchmark module
+
+        case_replay(vb)
+        return
     case_mt(tf, True, "fiber_mt")
     case_mt(tf, False, "plain_mt")
     case_ragged(tf, oracle)
@@ -293,6 +360,9 @@ def main():
     case_lowp(tf, torch.bfloat16, "bf16_params")
     case_lowp(tf, torch.float16, "f16_params")
     case_unit_linear(tf)
+    import vision_benchmark as vb
+
+    case_replay(vb)
 
 
 if __name__ == "__main__":
