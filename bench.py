@@ -60,6 +60,10 @@ def parse_args():
                     help="skip the nvidia-smi clock sampler (profiling runs)")
     ap.add_argument("--no-replay", action="store_true",
                     help="skip the replay-record codec measurement")
+    ap.add_argument("--replay-only", action="store_true",
+                    help="measure only the replay-record codec (one GPU) and print its JSON")
+    ap.add_argument("--replay-batch", type=int, default=65536,
+                    help="records per codec launch")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
     ap.add_argument("--transport", choices=("auto", "peer", "nvls", "nccl"), default="auto",
@@ -401,7 +405,8 @@ def run_single(args, device):
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": desc}
     if not args.no_replay:
-        line["replay"] = run_replay(device, peak, peak_kind, cpu=not args.no_cpu_baseline)
+        line["replay"] = run_replay(device, peak, peak_kind, n=args.replay_batch,
+                                    cpu=not args.no_cpu_baseline)
     return line
 
 
@@ -410,7 +415,7 @@ REPLAY_ENCODE_BYTES = 3072 * 4 + 8 + 1552   # image + label + task in, record ou
 REPLAY_DECODE_BYTES = 1552 + 3072 * 4 + 12  # record in, image + label + task + status out
 
 
-def run_replay(device, peak, peak_kind, cpu=True, reps=10):
+def run_replay(device, peak, peak_kind, n=REPLAY_BATCH, cpu=True, reps=10):
     """The replay-record codec (dfc_replay_encode / dfc_replay_decode) on a
     batch of 65,536 records, each launch timed with CUDA events on the
     launching stream; beside it the CPU codec (the oracle's restatement of
@@ -418,7 +423,6 @@ def run_replay(device, peak, peak_kind, cpu=True, reps=10):
     from oracle import replay as R
     from t3st_b200 import _lib
 
-    n = REPLAY_BATCH
     g = torch.Generator(device=device).manual_seed(3)
     x = torch.rand((n, 3072), generator=g, device=device)
     y = torch.randint(0, 100, (n,), generator=g, device=device, dtype=torch.int32)
@@ -440,7 +444,7 @@ def run_replay(device, peak, peak_kind, cpu=True, reps=10):
             meta[2].data_ptr(), stream.cuda_stream))
 
     res = {"batch_records": n, "launches_timed": 2 * reps,
-           "l2": "805 MB of images per launch > 126 MB L2 (no flush)"}
+           "l2": f"{n * 3072 * 4 / 1e6:.0f} MB of images per launch (L2 126 MB; no flush)"}
     for name, fn, nbytes in (("encode", enc, REPLAY_ENCODE_BYTES), ("decode", dec, REPLAY_DECODE_BYTES)):
         for _ in range(3):
             fn()
@@ -659,6 +663,12 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.replay_only:
+        if rank == 0:
+            peak, peak_kind = measured_hbm_peak()
+            print(json.dumps({"replay": run_replay(device, peak, peak_kind, n=args.replay_batch,
+                                                   cpu=not args.no_cpu_baseline)}), flush=True)
+        return
     if world == 1:
         line = run_single(args, device)
     else:

@@ -34,7 +34,7 @@ namespace dfc {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kVec = 8;                      // elements per thread per tile
+constexpr int kVec = 8;                      // elements per thread per tile (two quads)
 constexpr int kTile = kThreads * kVec;       // 2048 elements per CTA
 constexpr int kMaxPeers = DFC_MAX_PEERS;
 
@@ -44,7 +44,7 @@ struct PeerSegArg {
   uint32_t* m;
   uint32_t* v;
   int32_t hyper;
-  int32_t vec;     // offset and n allow the 8-wide path
+  int32_t vec;     // offset and moment words allow the quad path
 };
 
 template <int MAXS, int MAXH>
@@ -64,68 +64,6 @@ struct ZeroBatch {
 
 constexpr int kMaxSegs = 512, kMaxHypers = 16;
 static_assert(sizeof(ZeroBatch<kMaxSegs, kMaxHypers>) <= 32000, "launch parameter limit");
-
-__device__ __forceinline__ void bf16x8_add(float (&acc)[8], const uint4& c) {
-  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    acc[2 * k] = __fadd_rn(acc[2 * k], u2f(w[k] << 16));
-    acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], u2f(w[k] & 0xFFFF0000u));
-  }
-}
-
-// NP = number of ranks when known at compile time (2, 4, 8), 0 = any (up to
-// kMaxPeers, predicated).  All peer loads are issued before the first add so
-// the remote latencies overlap instead of adding up.
-template <int MODE, int NP, int MAXS, int MAXH>
-__device__ __forceinline__ void vec8(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
-                                     int64_t local, const Scalars& s) {
-  constexpr int kLoads = NP ? NP : kMaxPeers;
-  const int np = NP ? NP : b.n_peers;
-  const int64_t j = sg.offset + local;
-  uint4 c[kLoads];
-#pragma unroll
-  for (int q = 0; q < kLoads; ++q)
-    if (NP || q < np) c[q] = __ldcs(reinterpret_cast<const uint4*>(b.comp[q] + j));
-  float* mine = b.param[b.rank] + j;
-  float4 p0 = __ldcs(reinterpret_cast<const float4*>(mine));
-  float4 p1 = __ldcs(reinterpret_cast<const float4*>(mine + 4));
-  uint4 m0 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local));
-  uint4 m1 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local + 4));
-  uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local));
-  uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local + 4));
-  // g = comp_0[j], then + comp_q[j] for q = 1..N-1 (rank order)
-  float g[8];
-  const uint32_t w0[4] = {c[0].x, c[0].y, c[0].z, c[0].w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    g[2 * k] = u2f(w0[k] << 16);
-    g[2 * k + 1] = u2f(w0[k] & 0xFFFF0000u);
-  }
-#pragma unroll
-  for (int q = 1; q < kLoads; ++q)
-    if (NP || q < np) bf16x8_add(g, c[q]);
-  step_elem<MODE>(s, p0.x, g[0], m0.x, v0.x);
-  step_elem<MODE>(s, p0.y, g[1], m0.y, v0.y);
-  step_elem<MODE>(s, p0.z, g[2], m0.z, v0.z);
-  step_elem<MODE>(s, p0.w, g[3], m0.w, v0.w);
-  step_elem<MODE>(s, p1.x, g[4], m1.x, v1.x);
-  step_elem<MODE>(s, p1.y, g[5], m1.y, v1.y);
-  step_elem<MODE>(s, p1.z, g[6], m1.z, v1.z);
-  step_elem<MODE>(s, p1.w, g[7], m1.w, v1.w);
-  __stcs(reinterpret_cast<uint4*>(sg.m + local), m0);
-  __stcs(reinterpret_cast<uint4*>(sg.m + local + 4), m1);
-  __stcs(reinterpret_cast<uint4*>(sg.v + local), v0);
-  __stcs(reinterpret_cast<uint4*>(sg.v + local + 4), v1);
-#pragma unroll
-  for (int q = 0; q < kLoads; ++q) {
-    if (NP || q < np) {
-      float* dst = b.param[q] + j;
-      __stcs(reinterpret_cast<float4*>(dst), p0);
-      __stcs(reinterpret_cast<float4*>(dst + 4), p1);
-    }
-  }
-}
 
 // The switch's sum of element j over every rank: the aligned bf16x2 word
 // that holds j is reduced (FP32 accumulation, bf16 result) and j's half kept.
@@ -153,46 +91,93 @@ __device__ __forceinline__ void nvls_sum8(const uint16_t* mc, float (&g)[8]) {
   }
 }
 
-// NVLS (NVSwitch multicast): the switch sums the 8 bf16 values at comp_mc + j
-// of every rank with FP32 accumulation and returns them rounded to bf16; one
-// multicast store writes the new parameters into every rank's copy.  Each
-// value crosses this GPU's links once instead of once per peer.
-template <int MODE, int MAXS, int MAXH>
-__device__ __forceinline__ void vec8_nvls(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
-                                          int64_t local, const Scalars& s) {
-  const int64_t j = sg.offset + local;
-  float g[8];
-  nvls_sum8(b.comp_mc + j, g);
-  const float* mine = b.param[b.rank] + j;
-  float4 p0 = __ldcs(reinterpret_cast<const float4*>(mine));
-  float4 p1 = __ldcs(reinterpret_cast<const float4*>(mine + 4));
-  uint4 m0 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local));
-  uint4 m1 = __ldcs(reinterpret_cast<const uint4*>(sg.m + local + 4));
-  uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local));
-  uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(sg.v + local + 4));
-  step_elem<MODE>(s, p0.x, g[0], m0.x, v0.x);
-  step_elem<MODE>(s, p0.y, g[1], m0.y, v0.y);
-  step_elem<MODE>(s, p0.z, g[2], m0.z, v0.z);
-  step_elem<MODE>(s, p0.w, g[3], m0.w, v0.w);
-  step_elem<MODE>(s, p1.x, g[4], m1.x, v1.x);
-  step_elem<MODE>(s, p1.y, g[5], m1.y, v1.y);
-  step_elem<MODE>(s, p1.z, g[6], m1.z, v1.z);
-  step_elem<MODE>(s, p1.w, g[7], m1.w, v1.w);
-  __stcs(reinterpret_cast<uint4*>(sg.m + local), m0);
-  __stcs(reinterpret_cast<uint4*>(sg.m + local + 4), m1);
-  __stcs(reinterpret_cast<uint4*>(sg.v + local), v0);
-  __stcs(reinterpret_cast<uint4*>(sg.v + local + 4), v1);
-  float* dst = b.param_mc + j;
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-               "f"(p0.x), "f"(p0.y), "f"(p0.z), "f"(p0.w)
+__device__ __forceinline__ void nvls_sum4(const uint16_t* mc, float (&g)[4]) {
+  uint32_t r[2];
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v2.bf16x2 {%0, %1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "l"(mc)
                : "memory");
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4),
-               "f"(p1.x), "f"(p1.y), "f"(p1.z), "f"(p1.w)
-               : "memory");
+  g[0] = u2f(r[0] << 16);
+  g[1] = u2f(r[0] & 0xFFFF0000u);
+  g[2] = u2f(r[1] << 16);
+  g[3] = u2f(r[1] & 0xFFFF0000u);
+}
+
+// Q quads (4 consecutive elements each) of one segment per thread, at local
+// offsets l[0..Q).  Thread t of a CTA takes quads t and t + 256 of its tile,
+// so every warp-wide access -- above all the parameter stores that cross
+// NVLink -- covers 32 consecutive quads: whole 32-byte sectors, no
+// half-filled remote writes.  All remote loads of the Q quads are issued
+// before the first use so their latencies overlap.
+//
+// Plain form (NVLS false): g = comp_0[j] + comp_1[j] + ... in FP32, rank
+// order, over NP ranks (NP = 2, 4, 8 at compile time; 0 = any, predicated),
+// and the new parameters are stored to every rank's copy.  NVLS form: the
+// switch's sum (multimem.ld_reduce) and one multicast store (multimem.st).
+template <int MODE, int NP, bool NVLS, int Q, int MAXS, int MAXH>
+__device__ __forceinline__ void quads(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
+                                      const int64_t (&l)[Q], const Scalars& s) {
+  constexpr int kLoads = NVLS ? 1 : (NP ? NP : kMaxPeers);
+  const int np = NP ? NP : b.n_peers;
+  float g[Q][4];
+  uint2 c[Q][kLoads];
+#pragma unroll
+  for (int u = 0; u < Q; ++u) {
+    const int64_t j = sg.offset + l[u];
+    if (NVLS) {
+      nvls_sum4(b.comp_mc + j, g[u]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < kLoads; ++q)
+        if (NP || q < np) c[u][q] = __ldcs(reinterpret_cast<const uint2*>(b.comp[q] + j));
+    }
+  }
+  float4 p[Q];
+  uint4 m[Q], v[Q];
+#pragma unroll
+  for (int u = 0; u < Q; ++u) {
+    p[u] = __ldcs(reinterpret_cast<const float4*>(b.param[b.rank] + sg.offset + l[u]));
+    m[u] = __ldcs(reinterpret_cast<const uint4*>(sg.m + l[u]));
+    v[u] = __ldcs(reinterpret_cast<const uint4*>(sg.v + l[u]));
+  }
+#pragma unroll
+  for (int u = 0; u < Q; ++u) {
+    if (!NVLS) {
+      g[u][0] = u2f(c[u][0].x << 16);
+      g[u][1] = u2f(c[u][0].x & 0xFFFF0000u);
+      g[u][2] = u2f(c[u][0].y << 16);
+      g[u][3] = u2f(c[u][0].y & 0xFFFF0000u);
+#pragma unroll
+      for (int q = 1; q < kLoads; ++q) {
+        if (NP || q < np) {
+          g[u][0] = __fadd_rn(g[u][0], u2f(c[u][q].x << 16));
+          g[u][1] = __fadd_rn(g[u][1], u2f(c[u][q].x & 0xFFFF0000u));
+          g[u][2] = __fadd_rn(g[u][2], u2f(c[u][q].y << 16));
+          g[u][3] = __fadd_rn(g[u][3], u2f(c[u][q].y & 0xFFFF0000u));
+        }
+      }
+    }
+    step_elem<MODE>(s, p[u].x, g[u][0], m[u].x, v[u].x);
+    step_elem<MODE>(s, p[u].y, g[u][1], m[u].y, v[u].y);
+    step_elem<MODE>(s, p[u].z, g[u][2], m[u].z, v[u].z);
+    step_elem<MODE>(s, p[u].w, g[u][3], m[u].w, v[u].w);
+    __stcs(reinterpret_cast<uint4*>(sg.m + l[u]), m[u]);
+    __stcs(reinterpret_cast<uint4*>(sg.v + l[u]), v[u]);
+    const int64_t j = sg.offset + l[u];
+    if (NVLS) {
+      asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(b.param_mc + j),
+                   "f"(p[u].x), "f"(p[u].y), "f"(p[u].z), "f"(p[u].w)
+                   : "memory");
+    } else {
+#pragma unroll
+      for (int q = 0; q < (NP ? NP : kMaxPeers); ++q)
+        if (NP || q < np) __stcs(reinterpret_cast<float4*>(b.param[q] + j), p[u]);
+    }
+  }
 }
 
 // One element.  Plain form: peer loads, FP32 sum in rank order, peer stores.
-// NVLS form: the switch's sum and one multicast store, as in vec8_nvls, so
+// NVLS form: the switch's sum and one multicast store, as in quads, so
 // every element of a bucket follows the switch's rounding.
 template <int MODE, bool NVLS, int MAXS, int MAXH>
 __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const PeerSegArg& sg,
@@ -231,16 +216,16 @@ __global__ void __launch_bounds__(kThreads)
   const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
   const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
   const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
-  int64_t done = 0;
-  if (sg.vec) {
-    const int64_t nv = count / kVec;
-    for (int64_t k = threadIdx.x; k < nv; k += kThreads) {
-      if (NVLS) vec8_nvls<MODE>(b, sg, base + k * kVec, s);
-      else vec8<MODE, NP>(b, sg, base + k * kVec, s);
-    }
-    done = nv * kVec;
+  const int64_t nq = sg.vec ? count / 4 : 0;  // whole quads of this tile
+  const int64_t k0 = threadIdx.x, k1 = threadIdx.x + kThreads;
+  if (k1 < nq) {
+    const int64_t l[2] = {base + 4 * k0, base + 4 * k1};
+    quads<MODE, NP, NVLS, 2>(b, sg, l, s);
+  } else if (k0 < nq) {
+    const int64_t l[1] = {base + 4 * k0};
+    quads<MODE, NP, NVLS, 1>(b, sg, l, s);
   }
-  for (int64_t k = done + threadIdx.x; k < count; k += kThreads)
+  for (int64_t k = nq * 4 + threadIdx.x; k < count; k += kThreads)
     scalar1<MODE, NVLS>(b, sg, base + k, s);
 }
 
@@ -406,7 +391,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     a.m = s.exp_avg;
     a.v = s.exp_avg_sq;
     a.hyper = local[s.hyper];
-    a.vec = (s.offset % 8 == 0) && aligned(s.exp_avg, 16) && aligned(s.exp_avg_sq, 16);
+    a.vec = (s.offset % 4 == 0) && aligned(s.exp_avg, 16) && aligned(s.exp_avg_sq, 16);
     b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
     ++b.n_segs;
   }

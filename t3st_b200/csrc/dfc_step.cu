@@ -39,6 +39,11 @@ namespace {
 #ifndef DFC_STEP_MIN_BLOCKS
 #define DFC_STEP_MIN_BLOCKS 8
 #endif
+// resident CTAs per SM asked of the FP32-word kernels (modes PLAIN and
+// SIGNFIBER), whose arithmetic needs more registers than the packed one
+#ifndef DFC_STEP_MIN_BLOCKS_FP32
+#define DFC_STEP_MIN_BLOCKS_FP32 DFC_STEP_MIN_BLOCKS
+#endif
 constexpr int kThreads = DFC_STEP_THREADS;
 constexpr int kVec = 4;
 constexpr int kUnroll = DFC_STEP_UNROLL;
@@ -177,7 +182,8 @@ __device__ __forceinline__ void run_tile(const SegArg& sg, int64_t base, int64_t
 // holds segments of a single type combination, so the hot FP32 kernel keeps
 // its 32-register budget.
 template <int MODE, int GDT, int PDT, int MAXS, int MAXH>
-__global__ void __launch_bounds__(kThreads, DFC_STEP_MIN_BLOCKS)
+__global__ void __launch_bounds__(kThreads, MODE == DFC_MODE_PACKED ? DFC_STEP_MIN_BLOCKS
+                                                                  : DFC_STEP_MIN_BLOCKS_FP32)
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
   const int32_t t = static_cast<int32_t>(blockIdx.x);
   int lo = 0, hi = b.n_segs;  // tile_base[lo] <= t < tile_base[hi]
