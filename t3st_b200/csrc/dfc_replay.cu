@@ -12,7 +12,8 @@
 //                final value 0xFFFFFFFF) of bytes [0, 1544), little-endian
 //   [1548, 1552) zero
 //
-// One warp per record.  The warp stages the record in shared memory with
+// One warp per record at a time (a persistent grid of 8 CTAs per SM, each
+// warp looping over records).  The warp stages the record in shared memory with
 // coalesced 16-byte loads or stores, and splits the CRC: lane k runs the
 // table-driven CRC over its own 48-byte run of the record (lane 0 also over
 // the 8-byte header, starting from 0xFFFFFFFF; the others from 0), then
@@ -76,30 +77,35 @@ const Shifts& shifts() {
   return s;
 }
 
-// The byte-at-a-time table: entry t is the remainder of byte t shifted
-// through eight steps of the reflected polynomial division.
-__device__ __forceinline__ void build_table(uint32_t* table) {
-  for (int t = threadIdx.x; t < 256; t += blockDim.x) {
-    uint32_t c = static_cast<uint32_t>(t);
+// Slicing-by-4 tables: t[0][i] is the remainder of byte i shifted through
+// eight steps of the reflected polynomial division; t[k][i] is that of byte
+// i followed by k zero bytes, t[k][i] = (t[k-1][i] >> 8) ^ t[0][t[k-1][i] & 0xFF].
+// A 32-bit word x = c ^ (4 message bytes) then advances the remainder with
+// four independent lookups: t[3][x0] ^ t[2][x1] ^ t[1][x2] ^ t[0][x3].
+__device__ __forceinline__ void build_tables(uint32_t (*t)[256]) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    uint32_t c = static_cast<uint32_t>(i);
     for (int k = 0; k < 8; ++k) c = (c >> 1) ^ ((c & 1u) ? kPoly : 0u);
-    table[t] = c;
+    t[0][i] = c;
+  }
+  __syncthreads();
+  for (int k = 1; k < 4; ++k) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      t[k][i] = (t[k - 1][i] >> 8) ^ t[0][t[k - 1][i] & 0xFFu];
+    __syncthreads();
   }
 }
 
 // CRC-32 of the record staged at rec (bytes [0, 1544)), all 32 lanes.
-__device__ __forceinline__ uint32_t record_crc(const uint8_t* rec, const uint32_t* table,
+__device__ __forceinline__ uint32_t record_crc(const uint8_t* rec, const uint32_t (*t)[256],
                                                const Shifts& sh, int lane) {
   const int start = lane == 0 ? 0 : kHeader + kRun * lane;
   const int end = kHeader + kRun * (lane + 1);
   uint32_t c = lane == 0 ? 0xFFFFFFFFu : 0u;
   const uint32_t* w = reinterpret_cast<const uint32_t*>(rec + start);
   for (int i = 0; i < (end - start) / 4; ++i) {
-    uint32_t word = w[i];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      c = table[(c ^ word) & 0xFFu] ^ (c >> 8);
-      word >>= 8;
-    }
+    const uint32_t x = c ^ w[i];
+    c = t[3][x & 0xFFu] ^ t[2][(x >> 8) & 0xFFu] ^ t[1][(x >> 16) & 0xFFu] ^ t[0][x >> 24];
   }
   c = gf2_mulmod(c, sh.lane[lane]);
 #pragma unroll
@@ -107,10 +113,12 @@ __device__ __forceinline__ uint32_t record_crc(const uint8_t* rec, const uint32_
   return ~c;
 }
 
+// clamp(rint(x * 15), 0, 15): the conversion rounds to nearest even and
+// saturates to [0, 2^32 - 1] with NaN -> 0; the min clamps the top.
 __device__ __forceinline__ uint32_t quant4(float x) {
-  // rint: nearest, ties to even (torch.round); NaN fails both compares -> 0
-  const float r = rintf(__fmul_rn(x, 15.0f));
-  return r >= 15.0f ? 15u : (r > 0.0f ? static_cast<uint32_t>(r) : 0u);
+  uint32_t q;
+  asm("cvt.rni.sat.u32.f32 %0, %1;" : "=r"(q) : "f"(__fmul_rn(x, 15.0f)));
+  return min(q, 15u);
 }
 
 struct EncodeArgs {
@@ -124,39 +132,41 @@ struct EncodeArgs {
   Shifts sh;
 };
 
+// Persistent: each warp takes records warp, warp + W, ... (W = warps in the grid).
 __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant__ EncodeArgs a) {
-  __shared__ uint32_t table[256];
+  __shared__ uint32_t tables[4][256];
   __shared__ __align__(16) uint8_t stage[kWarps][kRecordBytes];
-  build_table(table);
-  __syncthreads();
+  build_tables(tables);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
-  if (r >= a.n) return;
   uint8_t* rec = stage[warp];
-  const float4* src = reinterpret_cast<const float4*>(a.images + r * a.image_stride);
   uint16_t* packed = reinterpret_cast<uint16_t*>(rec + kHeader);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < a.n; r += stride) {
+    const float4* src = reinterpret_cast<const float4*>(a.images + r * a.image_stride);
 #pragma unroll 4
-  for (int i = lane; i < kPixels / 4; i += 32) {
-    const float4 x = __ldg(src + i);
-    packed[i] = static_cast<uint16_t>(quant4(x.x) | (quant4(x.y) << 4) | (quant4(x.z) << 8) |
-                                      (quant4(x.w) << 12));
+    for (int i = lane; i < kPixels / 4; i += 32) {
+      const float4 x = __ldg(src + i);
+      packed[i] = static_cast<uint16_t>(quant4(x.x) | (quant4(x.y) << 4) | (quant4(x.z) << 8) |
+                                        (quant4(x.w) << 12));
+    }
+    if (lane == 0) {
+      const uint32_t y = static_cast<uint32_t>(a.labels[r]) & 0xFFFFu;
+      const uint32_t t = static_cast<uint32_t>(a.tasks[r]) & 0xFFFFu;
+      reinterpret_cast<uint32_t*>(rec)[0] = 0x42344643u;  // "CF4B"
+      reinterpret_cast<uint32_t*>(rec)[1] = y | (t << 16);
+    }
+    __syncwarp();
+    const uint32_t crc = record_crc(rec, tables, a.sh, lane);
+    if (lane == 0) {
+      reinterpret_cast<uint32_t*>(rec + kCrcBytes)[0] = crc;
+      reinterpret_cast<uint32_t*>(rec + kCrcBytes)[1] = 0u;
+    }
+    __syncwarp();
+    uint4* dst = reinterpret_cast<uint4*>(a.records + r * a.record_stride);
+    const uint4* s4 = reinterpret_cast<const uint4*>(rec);
+    for (int i = lane; i < kRecordBytes / 16; i += 32) dst[i] = s4[i];
+    __syncwarp();  // the stage is rewritten by the next record
   }
-  if (lane == 0) {
-    const uint32_t y = static_cast<uint32_t>(a.labels[r]) & 0xFFFFu;
-    const uint32_t t = static_cast<uint32_t>(a.tasks[r]) & 0xFFFFu;
-    reinterpret_cast<uint32_t*>(rec)[0] = 0x42344643u;  // "CF4B"
-    reinterpret_cast<uint32_t*>(rec)[1] = y | (t << 16);
-  }
-  __syncwarp();
-  const uint32_t crc = record_crc(rec, table, a.sh, lane);
-  if (lane == 0) {
-    reinterpret_cast<uint32_t*>(rec + kCrcBytes)[0] = crc;
-    reinterpret_cast<uint32_t*>(rec + kCrcBytes)[1] = 0u;
-  }
-  __syncwarp();
-  uint4* dst = reinterpret_cast<uint4*>(a.records + r * a.record_stride);
-  const uint4* s4 = reinterpret_cast<const uint4*>(rec);
-  for (int i = lane; i < kRecordBytes / 16; i += 32) dst[i] = s4[i];
 }
 
 struct DecodeArgs {
@@ -171,40 +181,56 @@ struct DecodeArgs {
 };
 
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeArgs a) {
-  __shared__ uint32_t table[256];
+  __shared__ uint32_t tables[4][256];
+  __shared__ float2 pair[256];  // byte -> (low nibble / 15, high nibble / 15)
   __shared__ __align__(16) uint8_t stage[kWarps][kRecordBytes];
-  build_table(table);
-  __syncthreads();
+  for (int t = threadIdx.x; t < 256; t += blockDim.x)
+    pair[t] = make_float2(__fdiv_rn(static_cast<float>(t & 15), 15.0f),
+                          __fdiv_rn(static_cast<float>(t >> 4), 15.0f));
+  build_tables(tables);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
-  if (r >= a.n) return;
   uint8_t* rec = stage[warp];
-  const uint4* src = reinterpret_cast<const uint4*>(a.records + r * a.record_stride);
   uint4* s4 = reinterpret_cast<uint4*>(rec);
-  for (int i = lane; i < kRecordBytes / 16; i += 32) s4[i] = __ldg(src + i);
-  __syncwarp();
-  const uint32_t crc = record_crc(rec, table, a.sh, lane);
   const uint16_t* packed = reinterpret_cast<const uint16_t*>(rec + kHeader);
-  float4* dst = reinterpret_cast<float4*>(a.images + r * kPixels);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < a.n; r += stride) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.records + r * a.record_stride);
+    for (int i = lane; i < kRecordBytes / 16; i += 32) s4[i] = __ldg(src + i);
+    __syncwarp();
+    // pixels first, so their stores drain while the CRC runs
+    float4* dst = reinterpret_cast<float4*>(a.images + r * kPixels);
 #pragma unroll 4
-  for (int i = lane; i < kPixels / 4; i += 32) {
-    const uint32_t b = packed[i];
-    dst[i] = make_float4(__fdiv_rn(static_cast<float>(b & 15u), 15.0f),
-                         __fdiv_rn(static_cast<float>((b >> 4) & 15u), 15.0f),
-                         __fdiv_rn(static_cast<float>((b >> 8) & 15u), 15.0f),
-                         __fdiv_rn(static_cast<float>(b >> 12), 15.0f));
-  }
-  if (lane == 0) {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(rec);
-    const uint32_t stored = reinterpret_cast<const uint32_t*>(rec + kCrcBytes)[0];
-    a.labels[r] = static_cast<int32_t>(w[1] & 0xFFFFu);
-    a.tasks[r] = static_cast<int32_t>(w[1] >> 16);
-    a.status[r] = w[0] != 0x42344643u ? DFC_RECORD_BAD_MAGIC
-                                      : (stored != crc ? DFC_RECORD_BAD_CRC : DFC_RECORD_OK);
+    for (int i = lane; i < kPixels / 4; i += 32) {
+      const uint32_t b = packed[i];
+      const float2 lo = pair[b & 0xFFu], hi = pair[b >> 8];
+      dst[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    const uint32_t crc = record_crc(rec, tables, a.sh, lane);
+    if (lane == 0) {
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(rec);
+      const uint32_t stored = reinterpret_cast<const uint32_t*>(rec + kCrcBytes)[0];
+      a.labels[r] = static_cast<int32_t>(w[1] & 0xFFFFu);
+      a.tasks[r] = static_cast<int32_t>(w[1] >> 16);
+      a.status[r] = w[0] != 0x42344643u ? DFC_RECORD_BAD_MAGIC
+                                        : (stored != crc ? DFC_RECORD_BAD_CRC : DFC_RECORD_OK);
+    }
+    __syncwarp();  // the stage is rewritten by the next record
   }
 }
 
-int64_t blocks_for(int64_t n) { return (n + kWarps - 1) / kWarps; }
+// One CTA per 8 records, at most as many CTAs as are resident at once (one
+// wave): SMs x resident CTAs per SM for this kernel.
+template <typename Kernel>
+int grid_for(Kernel kernel, int64_t n) {
+  int dev = 0, sms = 148, per_sm = 1;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t need = (n + kWarps - 1) / kWarps;
+  return static_cast<int>(std::min<int64_t>(need, static_cast<int64_t>(sms) * per_sm));
+}
 
 }  // namespace
 }  // namespace dfc
@@ -219,7 +245,6 @@ extern "C" int dfc_replay_encode(const float* images, int64_t image_stride, cons
   if (!aligned(images, 16) || image_stride % 4 != 0 || !aligned(records, 16) ||
       record_stride % 16 != 0 || !aligned(labels, 4) || !aligned(tasks, 4))
     return DFC_ERR_ALIGN;
-  if (blocks_for(n_records) > INT32_MAX) return DFC_ERR_SIZE;
   EncodeArgs a;
   a.images = images;
   a.image_stride = image_stride;
@@ -229,8 +254,7 @@ extern "C" int dfc_replay_encode(const float* images, int64_t image_stride, cons
   a.record_stride = record_stride;
   a.n = n_records;
   a.sh = shifts();
-  encode_kernel<<<static_cast<unsigned>(blocks_for(n_records)), kThreads, 0,
-                  static_cast<cudaStream_t>(stream)>>>(a);
+  encode_kernel<<<grid_for(encode_kernel, n_records), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 
@@ -244,7 +268,6 @@ extern "C" int dfc_replay_decode(const uint8_t* records, int64_t record_stride, 
   if (!aligned(records, 16) || record_stride % 16 != 0 || !aligned(images, 16) ||
       !aligned(labels, 4) || !aligned(tasks, 4) || !aligned(status, 4))
     return DFC_ERR_ALIGN;
-  if (blocks_for(n_records) > INT32_MAX) return DFC_ERR_SIZE;
   DecodeArgs a;
   a.records = records;
   a.record_stride = record_stride;
@@ -254,7 +277,6 @@ extern "C" int dfc_replay_decode(const uint8_t* records, int64_t record_stride, 
   a.status = status;
   a.n = n_records;
   a.sh = shifts();
-  decode_kernel<<<static_cast<unsigned>(blocks_for(n_records)), kThreads, 0,
-                  static_cast<cudaStream_t>(stream)>>>(a);
+  decode_kernel<<<grid_for(decode_kernel, n_records), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }

@@ -42,7 +42,7 @@ namespace {
 // resident CTAs per SM asked of the FP32-word kernels (modes PLAIN and
 // SIGNFIBER), whose arithmetic needs more registers than the packed one
 #ifndef DFC_STEP_MIN_BLOCKS_FP32
-#define DFC_STEP_MIN_BLOCKS_FP32 DFC_STEP_MIN_BLOCKS
+#define DFC_STEP_MIN_BLOCKS_FP32 6
 #endif
 constexpr int kThreads = DFC_STEP_THREADS;
 constexpr int kVec = 4;
