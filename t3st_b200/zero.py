@@ -86,12 +86,14 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     "peer": one fused kernel over NVLink peer memory
                     (dfc_zero_fused_step) between two cross-GPU barriers;
                     needs symmetric memory and compressed gradients;
-                    "auto" (default): "peer" for 2 ranks, "nccl" for more --
-                    measured on B200 over a 2^30-element vector: 2 ranks
-                    7.6 ms (peer) vs 10.5 ms (nccl); 4 ranks 13.7 vs 11.1;
-                    8 ranks 16.3 vs 11.3 (the fused kernel sends every
-                    parameter to each peer with plain stores, NCCL does
-                    better once there are more than two ranks)
+                    "nvls": the same kernel with the reduction and the
+                    parameter broadcast done by the NVSwitch (multimem);
+                    needs NVLink multicast;
+                    "auto" (default): the measured fastest -- on B200 over a
+                    2^30-element vector, ms per step (peer / nvls / nccl):
+                    2 ranks 6.5 / 10.0 / 10.5; 4 ranks - / 9.1 / 11.2;
+                    8 ranks 10.0 / 9.1 / 11.2.  So peer at 2 ranks, nvls
+                    from 4 on (nccl where the node has no multicast)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -119,9 +121,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         if transport not in ("auto", "nccl", "peer", "nvls"):
             raise ValueError("transport must be 'auto', 'nccl', 'peer' or 'nvls'")
         if transport == "auto":
-            on_cuda = all(p.is_cuda for g in self.param_groups for p in g["params"])
-            fused_ok = self.world == 2 and self.compress and backend is None and on_cuda
-            transport = "peer" if fused_ok else "nccl"
+            transport = self._auto_transport(backend)
         self.transport = transport if self.world > 1 else "nccl"
         if self.transport in ("peer", "nvls") and not self.compress:
             raise ValueError("the peer and nvls transports reduce bf16 compressed gradients")
@@ -129,6 +129,24 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self._layout(bucket_elems)
         if self.transport in ("peer", "nvls"):
             self._setup_peer()
+
+    def _auto_transport(self, backend) -> str:
+        """The measured fastest on B200 over a 2^30-element vector: the
+        peer-memory kernel at 2 ranks; the NVSwitch-multicast kernel from 4
+        ranks on where the node has NVLink multicast; NCCL otherwise (or for
+        uncompressed gradients, a custom backend or non-CUDA parameters)."""
+        params = [p for g in self.param_groups for p in g["params"]]
+        if self.world < 2 or not self.compress or backend is not None or \
+                not all(p.is_cuda for p in params):
+            return "nccl"
+        if self.world == 2:
+            return "peer"
+        from torch._C._autograd import DeviceType
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        if _SymmetricMemory.has_multicast_support(DeviceType.CUDA, params[0].device.index):
+            return "nvls"
+        return "nccl"
 
     # ---- layout -----------------------------------------------------------
     @torch.no_grad()

@@ -149,22 +149,38 @@ def _multicast_ok() -> bool:
     return _SymmetricMemory.has_multicast_support(DeviceType.CUDA, 0)
 
 
+def _spawn(world, transport):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, transport, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert results[r] == "ok", results[r]
+
+
 @pytest.mark.parametrize("transport", ["nccl", "peer", "nvls"])
 def test_sharded_on_two_gpus(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
-    import torch.multiprocessing as mp
+    _spawn(2, transport)
 
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    results = dict(q.get(timeout=300) for _ in range(2))
-    for p in procs:
-        p.join(timeout=60)
-    for r in range(2):
-        assert results[r] == "ok", results[r]
+
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "nvls"])
+def test_sharded_on_more_gpus(transport, world):
+    """The same check with 4 and 8 ranks (the switch then sums 4 or 8 values
+    per element, and the fused kernel reads and writes 3 or 7 peers)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if transport == "nvls" and not _multicast_ok():
+        pytest.skip("no NVLink multicast on this node")
+    _spawn(world, transport)
