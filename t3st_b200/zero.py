@@ -144,9 +144,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         from torch._C._autograd import DeviceType
         from torch._C._distributed_c10d import _SymmetricMemory
 
-        if _SymmetricMemory.has_multicast_support(DeviceType.CUDA, params[0].device.index):
-            return "nvls"
-        return "nccl"
+        try:
+            multicast = _SymmetricMemory.has_multicast_support(DeviceType.CUDA,
+                                                               params[0].device.index)
+        except RuntimeError:  # no CUDA driver to ask
+            multicast = False
+        return "nvls" if multicast else "nccl"
 
     # ---- layout -----------------------------------------------------------
     @torch.no_grad()

@@ -208,3 +208,31 @@ def test_lost_rank_surfaces_as_error_not_hang():
             p.kill()
     assert results[1] == "left"
     assert results[0].startswith("error"), results[0]
+
+
+def test_auto_transport_choice():
+    """The automatic transport: NCCL for one rank, uncompressed gradients,
+    a custom backend or CPU tensors; the peer kernel at 2 ranks; the
+    multicast kernel from 4 ranks only where the node reports NVLink
+    multicast (never on a machine without a CUDA driver)."""
+    import types
+
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    class FakeParam:
+        is_cuda = True
+        device = types.SimpleNamespace(index=0)
+
+    def choose(world, compress=True, backend=None, cuda=True):
+        stub = types.SimpleNamespace(world=world, compress=compress,
+                                     param_groups=[{"params": [FakeParam() if cuda else
+                                                               torch.zeros(1)]}])
+        return ShardedDFCAdamW._auto_transport(stub, backend)
+
+    assert choose(1) == "nccl"
+    assert choose(2) == "peer"
+    assert choose(2, compress=False) == "nccl"
+    assert choose(2, backend=object()) == "nccl"
+    assert choose(4, cuda=False) == "nccl"
+    if not torch.cuda.is_available():
+        assert choose(8) == "nccl"
