@@ -270,26 +270,32 @@ def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None =
 
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU path (restated as torch CPU ops)
-    on the host cores, rank 0 only, K+W bounded steps."""
+    on the host cores, rank 0 only, K+W bounded steps.  At N=1 the sample is
+    a prefix of the ResNet-18 tensors; at N>1 a prefix of the flat 2^30-element
+    ZeRO-1 vector (the reference has no distributed code: its step over the
+    whole vector on one host is the comparison)."""
     if rank != 0:
         return
     from oracle import torch_port
     from t3st_b200.workloads import resnet18_cifar_shapes
 
-    shapes = resnet18_cifar_shapes()
+    shapes = resnet18_cifar_shapes() if world == 1 else [(ZERO_PARAMS,)]
     torch.set_num_threads(os.cpu_count() or 1)
     total_params = sum(math.prod(s) for s in shapes)
-    # calibrate on one full step, then bound the sample so the run takes <~2 min
-    rate_full, _, _ = cpu_port_rate(shapes, 0.5, packed=True)
+    # calibrate on the ResNet-18 step, then bound the sample so the run takes <~2 min
+    rate_full, _, _ = cpu_port_rate(resnet18_cifar_shapes(), 0.5, packed=True)
     budget = 120.0
     per_step = budget / max(1, args.steps + args.warmup)
-    max_params = max(4096, min(total_params, int(rate_full * per_step)))
+    # and to at most 2^25 elements (512 MB of host state): the CPU rate per
+    # element does not depend on the sample size
+    max_params = max(4096, min(total_params, int(rate_full * per_step), 1 << 25))
     gen = torch.Generator().manual_seed(1)
     tensors, total = [], 0
     for s in shapes:
         n = math.prod(s)
         if tensors and total + n > max_params:
             break
+        n = min(n, max_params)  # the flat vector: a prefix
         tensors.append((torch.randn(n, generator=gen) * 0.02, torch.randn(n, generator=gen) * 1e-3,
                         torch.zeros(n, dtype=torch.int32), torch.zeros(n, dtype=torch.int32)))
         total += n
@@ -305,17 +311,24 @@ def run_reference(args, rank, world):
             torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
     el = time.perf_counter() - t0
     value = total * args.steps / el
-    sample = (f"{len(tensors)} of {len(shapes)} ResNet-18 (CIFAR) tensors, {total} of "
-              f"{total_params} params per step, packed moments, torch CPU ops")
+    if world == 1:
+        sample = (f"{len(tensors)} of {len(shapes)} ResNet-18 (CIFAR) tensors, {total} of "
+                  f"{total_params} params per step, packed moments, torch CPU ops")
+        workload = "resnet18-cifar multi-tensor DFC-AdamW step (reference CPU path)"
+    else:
+        sample = (f"first {total} of the {total_params} elements of the flat vector per step, "
+                  f"packed moments, torch CPU ops")
+        workload = ("flat 2^30-element FP32 vector DFC-AdamW step on one host "
+                    "(reference CPU path; the reference has no distributed code)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "resnet18-cifar multi-tensor DFC-AdamW step (reference CPU path)",
-                   "tensors": len(shapes), "params": total_params, "moment_format": "packed"},
+        "config": {"workload": workload, "tensors": len(shapes), "params": total_params,
+                   "moment_format": "packed"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -396,6 +409,7 @@ def run_single(args, device):
         "host_wall_ms_per_step": wall / K * 1e3,
     }
 
+    line["reference_default_format"] = run_fp32_format(args, device, peak)
     if not args.no_host_overhead:
         line["host_us_per_step"] = host_overhead_us(opt)
     if not args.no_e2e:
@@ -403,7 +417,7 @@ def run_single(args, device):
     if not args.no_cpu_baseline:
         rate, desc, cores = cpu_port_rate(resnet18_cifar_shapes(), args.cpu_seconds, packed=True)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": desc}
+                                "sample": desc, "cpu_model": cpu_model()}
     if not args.no_replay:
         line["replay"] = run_replay(device, peak, peak_kind, n=args.replay_batch,
                                     cpu=not args.no_cpu_baseline)
@@ -475,6 +489,46 @@ def run_replay(device, peak, peak_kind, n=REPLAY_BATCH, cpu=True, reps=10):
                                "kind": "port",
                                "sample": f"{k} records through the numpy + zlib codec"}
     return res
+
+
+def run_fp32_format(args, device, peak, K=300):
+    """The same step in the reference's own moment format (FP32 words, sign
+    fiber on: DFCAdamW's defaults), timed the same way."""
+    from t3st_b200 import DFCAdamW
+
+    params, _, _, gen, n_params = resnet18_params(device, seed=1)
+    opt = DFCAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD)
+    for _ in range(10):
+        fill_grads(params, gen)
+        opt.step()
+    fill_grads(params, gen)
+    for _ in range(max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    gbs = STEP_BYTES_PER_PARAM * n_params / (ms / 1e3) / 1e9
+    return {"moment_format": "fp32", "enable_fiber": True, "value": n_params / (ms / 1e3),
+            "unit": UNIT, "ms_per_step": ms, "steps": K, "hbm_gbs": gbs,
+            "frac_of_measured_hbm": gbs / peak,
+            "kernel": "dfc::step_kernel<SIGNFIBER> (6 CTAs/SM)"}
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K):
