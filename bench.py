@@ -225,12 +225,15 @@ def fill_grads(params, gen, std=1e-3):
 # ----------------------------------------------------------------------------
 # CPU baseline (reference algorithm as PyTorch CPU ops; oracle/torch_port.py)
 # ----------------------------------------------------------------------------
-def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None = None):
+def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None = None,
+                  threads: int | None = None, fiber: bool = True):
     """Time the reference step restated as CPU torch ops on (a prefix of)
-    the workload's tensors; returns (updates/s, description)."""
+    the workload's tensors; returns (updates/s, description, threads).
+    packed=False is the reference's own algorithm (remote/torch_fiber.py:
+    68-117, FP32 moments, sign fiber on unless fiber=False)."""
     from oracle import torch_port
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(threads or os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(1)
     tensors = []
     total = 0
@@ -250,7 +253,7 @@ def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None =
             if packed:
                 torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
             else:
-                torch_port.step_fp32(p, g, m, v, LR, BETAS, EPS, WD, step, fiber=True)
+                torch_port.step_fp32(p, g, m, v, LR, BETAS, EPS, WD, step, fiber=fiber)
 
     one(1)
     t0 = time.perf_counter()
@@ -262,18 +265,36 @@ def cpu_port_rate(shapes, seconds: float, packed: bool, max_params: int | None =
         if el >= seconds or (steps >= 3 and el * (steps + 1) / steps > 3 * seconds):
             break
     rate = total * steps / el
+    fmt = "packed" if packed else ("fp32 sign-fiber" if fiber else "fp32 fiber-off")
     desc = (f"{len(tensors)} of {len(shapes)} ResNet-18 tensors ({total} params), {steps} "
-            f"steps, {'packed' if packed else 'fp32 sign-fiber'} moments, "
-            f"{torch.get_num_threads()} threads")
-    return rate, desc, torch.get_num_threads()
+            f"steps, {fmt} moments, {torch.get_num_threads()} threads")
+    nthreads = torch.get_num_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    return rate, desc, nthreads
+
+
+def cpu_variants(shapes, seconds: float):
+    """The reference CPU step in its other settings: fiber off, one thread,
+    and the packed-word restatement (a format the reference lacks)."""
+    out = []
+    for packed, fiber, threads in ((False, False, None), (False, True, 1), (False, False, 1),
+                                   (True, True, None)):
+        rate, desc, nt = cpu_port_rate(shapes, seconds, packed=packed, threads=threads,
+                                       fiber=fiber)
+        out.append({"moment_format": "packed" if packed else "fp32", "enable_fiber": fiber,
+                    "threads": nt, "value": rate, "unit": UNIT, "sample": desc})
+    return out
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU path (restated as torch CPU ops)
-    on the host cores, rank 0 only, K+W bounded steps.  At N=1 the sample is
-    a prefix of the ResNet-18 tensors; at N>1 a prefix of the flat 2^30-element
-    ZeRO-1 vector (the reference has no distributed code: its step over the
-    whole vector on one host is the comparison)."""
+    """--impl reference: the reference's CPU path (remote/torch_fiber.py:
+    68-117 restated op for op as torch CPU ops, bit-identical to it: FP32
+    moments, sign fiber on, the reference's defaults) on the host cores,
+    rank 0 only, K+W bounded steps.  The reference has no packed moment
+    format; its FP32 path gives the same trajectory bit for bit.  At N=1 the
+    sample is a prefix of the ResNet-18 tensors; at N>1 a prefix of the flat
+    2^30-element ZeRO-1 vector (the reference has no distributed code: its
+    step over the whole vector on one host is the comparison)."""
     if rank != 0:
         return
     from oracle import torch_port
@@ -283,7 +304,7 @@ def run_reference(args, rank, world):
     torch.set_num_threads(os.cpu_count() or 1)
     total_params = sum(math.prod(s) for s in shapes)
     # calibrate on the ResNet-18 step, then bound the sample so the run takes <~2 min
-    rate_full, _, _ = cpu_port_rate(resnet18_cifar_shapes(), 0.5, packed=True)
+    rate_full, _, _ = cpu_port_rate(resnet18_cifar_shapes(), 0.5, packed=False)
     budget = 120.0
     per_step = budget / max(1, args.steps + args.warmup)
     # and to at most 2^25 elements (512 MB of host state): the CPU rate per
@@ -297,27 +318,27 @@ def run_reference(args, rank, world):
             break
         n = min(n, max_params)  # the flat vector: a prefix
         tensors.append((torch.randn(n, generator=gen) * 0.02, torch.randn(n, generator=gen) * 1e-3,
-                        torch.zeros(n, dtype=torch.int32), torch.zeros(n, dtype=torch.int32)))
+                        torch.zeros(n), torch.zeros(n)))
         total += n
     step = 0
     for _ in range(args.warmup):
         step += 1
         for p, g, m, v in tensors:
-            torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
+            torch_port.step_fp32(p, g, m, v, LR, BETAS, EPS, WD, step, fiber=True)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step += 1
         for p, g, m, v in tensors:
-            torch_port.step_packed(p, g, m, v, LR, BETAS, EPS, WD, step)
+            torch_port.step_fp32(p, g, m, v, LR, BETAS, EPS, WD, step, fiber=True)
     el = time.perf_counter() - t0
     value = total * args.steps / el
     if world == 1:
         sample = (f"{len(tensors)} of {len(shapes)} ResNet-18 (CIFAR) tensors, {total} of "
-                  f"{total_params} params per step, packed moments, torch CPU ops")
+                  f"{total_params} params per step, FP32 sign-fiber moments, torch CPU ops")
         workload = "resnet18-cifar multi-tensor DFC-AdamW step (reference CPU path)"
     else:
         sample = (f"first {total} of the {total_params} elements of the flat vector per step, "
-                  f"packed moments, torch CPU ops")
+                  f"FP32 sign-fiber moments, torch CPU ops")
         workload = ("flat 2^30-element FP32 vector DFC-AdamW step on one host "
                     "(reference CPU path; the reference has no distributed code)")
     line = {
@@ -326,7 +347,8 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": workload, "tensors": len(shapes), "params": total_params,
-                   "moment_format": "packed"},
+                   "moment_format": "fp32 sign-fiber (the reference's own format; it has no "
+                                    "packed format, and both give the same trajectory)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -415,9 +437,12 @@ def run_single(args, device):
     if not args.no_e2e:
         line["e2e"] = run_e2e(opt, params, flat_p, flat_g, gen, n_params, device, K)
     if not args.no_cpu_baseline:
-        rate, desc, cores = cpu_port_rate(resnet18_cifar_shapes(), args.cpu_seconds, packed=True)
+        rate, desc, cores = cpu_port_rate(resnet18_cifar_shapes(), args.cpu_seconds, packed=False)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": desc, "cpu_model": cpu_model()}
+                                "sample": desc + " (the reference's own format and defaults)",
+                                "cpu_model": cpu_model(),
+                                "variants": cpu_variants(resnet18_cifar_shapes(),
+                                                         args.cpu_seconds / 4)}
     if not args.no_replay:
         line["replay"] = run_replay(device, peak, peak_kind, n=args.replay_batch,
                                     cpu=not args.no_cpu_baseline)
