@@ -69,6 +69,10 @@ def parse_args():
     ap.add_argument("--transport", choices=("auto", "peer", "nvls", "nccl"), default="auto",
                     help="N>1: fused kernel over NVLink peer memory, the same kernel over "
                          "NVSwitch multicast, NCCL collectives, or the measured fastest for N")
+    ap.add_argument("--fused-ctas", type=int, default=None,
+                    help="N>1 peer/nvls: CTAs per SM of the fused kernel (0: one per tile)")
+    ap.add_argument("--compress-ctas", type=int, default=None,
+                    help="N>1 peer/nvls: CTAs per SM of the compression beside it (0: 8)")
     return ap.parse_args()
 
 
@@ -632,7 +636,9 @@ def run_sharded(args, rank, world, device):
     gen = torch.Generator(device=device).manual_seed(1234)  # same params on every rank
     param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
     opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
-                          moment_format="packed", transport=args.transport)
+                          moment_format="packed", transport=args.transport,
+                          fused_ctas_per_sm=args.fused_ctas,
+                          compress_ctas_per_sm=args.compress_ctas)
     del param
     ggen = torch.Generator(device=device).manual_seed(100 + rank)  # per-rank gradients
     opt.flat_grad[:P].normal_(0.0, 1e-3, generator=ggen)
@@ -683,6 +689,8 @@ def run_sharded(args, rank, world, device):
                             "step + all-gather)",
                 "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
                 "transport": opt.transport,
+                "fused_ctas_per_sm": opt.fused_ctas,
+                "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
             },
             "roofline": {"bound": "nvlink" if t_nvl > t_hbm else "hbm",

@@ -186,9 +186,12 @@ DFC_API int dfc_unpack_moments(uint32_t* words, int64_t n, int32_t second, void*
  * the previous call and recovered exactly from (comp, resid); comp <- s
  * rounded to the nearest bf16 (ties away from zero); resid <- the signed
  * 16-bit residual field.  comp and resid are read and written in place;
- * both start at zero.
+ * both start at zero.  ctas_per_sm (1..8; <= 0 means 8) caps the grid at
+ * that many 256-thread CTAs per SM, leaving room for a kernel that runs
+ * beside it on another stream (the ZeRO-1 pipeline's fused step).
  */
-DFC_API int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resid, int64_t n, void* stream);
+DFC_API int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resid, int64_t n,
+                            int32_t ctas_per_sm, void* stream);
 
 /*
  * Per-buffer gradient statistics with warp-shuffle block reductions and a
@@ -288,12 +291,16 @@ DFC_API int dfc_replay_decode(const uint8_t* records, int64_t record_stride, int
  * dfc_multicast_sum_bf16 returns the g values the switch produces.
  * The caller brackets the call with dfc_peer_barrier: before it so every
  * rank's gradients are complete, after it so every rank's parameters are.
+ * ctas_per_sm <= 0: one CTA per 2048-element tile; > 0: a persistent grid of
+ * at most that many CTAs per SM, so that the next bucket's dfc_compress_ef
+ * (with its own cap) runs beside it instead of after it.
  */
 DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
                                 const void* comp_multicast, void* param_multicast,
                                 int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                 int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
-                                int32_t mode, const float* device_grad_scale, void* stream);
+                                int32_t mode, const float* device_grad_scale,
+                                int32_t ctas_per_sm, void* stream);
 
 /*
  * The NVSwitch sum over every rank of numel bf16 values at a multicast

@@ -99,14 +99,15 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_mt_step": ([P, I32, P, I32, I32, P, P], ctypes.c_int),
         "dfc_pack_moments": ([P, I64, I32, P], ctypes.c_int),
         "dfc_unpack_moments": ([P, I64, I32, P], ctypes.c_int),
-        "dfc_compress_ef": ([P, P, P, I64, P], ctypes.c_int),
+        "dfc_compress_ef": ([P, P, P, I64, I32, P], ctypes.c_int),
         "dfc_grad_stats_scratch_bytes": ([P, I32], SZ),
         "dfc_grad_stats": ([P, I32, P, P, SZ, P], ctypes.c_int),
         "dfc_clip_coef": ([P, I32, ctypes.c_float, P, P, P], ctypes.c_int),
         "dfc_fiber_read": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_fiber_write": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
-        "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P], ctypes.c_int),
+        "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, I32, P],
+                                ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
         "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
         "dfc_replay_encode": ([P, I64, P, P, I64, P, I64, P], ctypes.c_int),

@@ -1,12 +1,34 @@
-// Version, status strings and the per-thread CUDA error slot of the C ABI.
+// Version, status strings, the per-thread CUDA error slot of the C ABI and
+// the SM-count cache used to size persistent grids.
+#include <atomic>
+
 #include "dfc_common.cuh"
 
 namespace dfc {
 namespace {
 thread_local int g_last_cuda_error = 0;
+constexpr int kMaxDevices = 256;
+std::atomic<int> g_sm_count[kMaxDevices];  // 0 until read
 }  // namespace
 
 void set_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return 148;
+  }
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return 148;
+    }
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 
 }  // namespace dfc
 

@@ -12,6 +12,9 @@ namespace dfc {
 // Status of the last CUDA failure on this host thread (dfc_last_cuda_error).
 void set_cuda_error(cudaError_t e);
 
+// Number of SMs of the current device (read once per device, then cached).
+int sm_count();
+
 // Check for a launch error after queueing kernels.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -55,17 +55,20 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-int grid_for(int64_t work) {
-  // Enough CTAs for 8 per SM on 148 SMs; fewer for small buffers.
+// ctas_per_sm CTAs per SM (8, the whole SM at 256 threads, by default);
+// fewer for small buffers.  A smaller figure leaves room on every SM for a
+// kernel that runs beside this one (the ZeRO-1 fused step).
+int grid_for(int64_t work, int32_t ctas_per_sm) {
+  const int64_t per_sm = ctas_per_sm > 0 ? std::min(ctas_per_sm, 8) : 8;
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + kThreads - 1) / kThreads,
-                                                                  148 * 8)));
+                                                                  sm_count() * per_sm)));
 }
 
 }  // namespace
 }  // namespace dfc
 
 extern "C" int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resid, int64_t n,
-                               void* stream) {
+                               int32_t ctas_per_sm, void* stream) {
   using namespace dfc;
   if (n < 0) return DFC_ERR_SIZE;
   if (n == 0) return DFC_OK;
@@ -75,10 +78,10 @@ extern "C" int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resi
   int64_t done = 0;
   if (aligned(grad, 16) && aligned(comp, 8) && aligned(resid, 8)) {
     const int64_t n4 = n / 4;
-    if (n4 > 0) compress_vec_kernel<<<grid_for(n4), kThreads, 0, st>>>(grad, comp, resid, n4);
+    if (n4 > 0) compress_vec_kernel<<<grid_for(n4, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, n4);
     done = n4 * 4;
   }
   if (done < n)
-    compress_scalar_kernel<<<grid_for(n - done), kThreads, 0, st>>>(grad, comp, resid, done, n);
+    compress_scalar_kernel<<<grid_for(n - done, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, done, n);
   return launch_status();
 }

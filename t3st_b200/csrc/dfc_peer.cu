@@ -203,54 +203,62 @@ __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const Pe
   }
 }
 
+// CTA c handles tiles c, c + gridDim.x, ...: one tile per CTA when the grid
+// has a CTA per tile, a persistent walk when the grid is capped so that a
+// kernel on another stream (the next bucket's compression) keeps SMs.
 template <int MODE, int NP, bool NVLS, int MAXS, int MAXH>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
-  const int32_t t = static_cast<int32_t>(blockIdx.x);
-  int lo = 0, hi = b.n_segs;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
+  const int32_t tiles = b.tile_base[b.n_segs];
+  for (int32_t t = static_cast<int32_t>(blockIdx.x); t < tiles; t += static_cast<int32_t>(gridDim.x)) {
+    int lo = 0, hi = b.n_segs;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
+    }
+    const PeerSegArg& sg = b.seg[lo];
+    const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
+    const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+    const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
+    const int64_t nq = sg.vec ? count / 4 : 0;  // whole quads of this tile
+    const int64_t k0 = threadIdx.x, k1 = threadIdx.x + kThreads;
+    if (k1 < nq) {
+      const int64_t l[2] = {base + 4 * k0, base + 4 * k1};
+      quads<MODE, NP, NVLS, 2>(b, sg, l, s);
+    } else if (k0 < nq) {
+      const int64_t l[1] = {base + 4 * k0};
+      quads<MODE, NP, NVLS, 1>(b, sg, l, s);
+    }
+    for (int64_t k = nq * 4 + threadIdx.x; k < count; k += kThreads)
+      scalar1<MODE, NVLS>(b, sg, base + k, s);
   }
-  const PeerSegArg& sg = b.seg[lo];
-  const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
-  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
-  const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
-  const int64_t nq = sg.vec ? count / 4 : 0;  // whole quads of this tile
-  const int64_t k0 = threadIdx.x, k1 = threadIdx.x + kThreads;
-  if (k1 < nq) {
-    const int64_t l[2] = {base + 4 * k0, base + 4 * k1};
-    quads<MODE, NP, NVLS, 2>(b, sg, l, s);
-  } else if (k0 < nq) {
-    const int64_t l[1] = {base + 4 * k0};
-    quads<MODE, NP, NVLS, 1>(b, sg, l, s);
-  }
-  for (int64_t k = nq * 4 + threadIdx.x; k < count; k += kThreads)
-    scalar1<MODE, NVLS>(b, sg, base + k, s);
 }
 
 template <int MODE, int MAXS, int MAXH>
-void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t tiles, cudaStream_t st) {
+void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t grid, cudaStream_t st) {
   if (b.comp_mc) {
-    zero_step_kernel<MODE, 0, true><<<tiles, kThreads, 0, st>>>(b);
+    zero_step_kernel<MODE, 0, true><<<grid, kThreads, 0, st>>>(b);
     return;
   }
   switch (b.n_peers) {
-    case 2: zero_step_kernel<MODE, 2, false><<<tiles, kThreads, 0, st>>>(b); break;
-    case 4: zero_step_kernel<MODE, 4, false><<<tiles, kThreads, 0, st>>>(b); break;
-    case 8: zero_step_kernel<MODE, 8, false><<<tiles, kThreads, 0, st>>>(b); break;
-    default: zero_step_kernel<MODE, 0, false><<<tiles, kThreads, 0, st>>>(b); break;
+    case 2: zero_step_kernel<MODE, 2, false><<<grid, kThreads, 0, st>>>(b); break;
+    case 4: zero_step_kernel<MODE, 4, false><<<grid, kThreads, 0, st>>>(b); break;
+    case 8: zero_step_kernel<MODE, 8, false><<<grid, kThreads, 0, st>>>(b); break;
+    default: zero_step_kernel<MODE, 0, false><<<grid, kThreads, 0, st>>>(b); break;
   }
 }
 
+// One CTA per tile (ctas_per_sm <= 0), or at most ctas_per_sm CTAs per SM.
 template <int MAXS, int MAXH>
-int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, cudaStream_t st) {
+int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, int32_t ctas_per_sm, cudaStream_t st) {
   const int32_t tiles = b.tile_base[b.n_segs];
   if (tiles == 0) return DFC_OK;
+  int32_t grid = tiles;
+  if (ctas_per_sm > 0) grid = static_cast<int32_t>(std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * ctas_per_sm));
   switch (mode) {
-    case DFC_MODE_PLAIN: launch_np<DFC_MODE_PLAIN>(b, tiles, st); break;
-    case DFC_MODE_SIGNFIBER: launch_np<DFC_MODE_SIGNFIBER>(b, tiles, st); break;
-    default: launch_np<DFC_MODE_PACKED>(b, tiles, st); break;
+    case DFC_MODE_PLAIN: launch_np<DFC_MODE_PLAIN>(b, grid, st); break;
+    case DFC_MODE_SIGNFIBER: launch_np<DFC_MODE_SIGNFIBER>(b, grid, st); break;
+    default: launch_np<DFC_MODE_PACKED>(b, grid, st); break;
   }
   return launch_status();
 }
@@ -327,7 +335,8 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
                                    const void* comp_multicast, void* param_multicast,
                                    int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                    int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
-                                   int32_t mode, const float* device_grad_scale, void* stream) {
+                                   int32_t mode, const float* device_grad_scale,
+                                   int32_t ctas_per_sm, void* stream) {
   using namespace dfc;
   if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers) return DFC_ERR_SIZE;
   if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
@@ -376,7 +385,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     const bool need = local[s.hyper] < 0;
     if (b.n_segs == kMaxSegs || (need && static_cast<int>(used.size()) == kMaxHypers) ||
         b.tile_base[b.n_segs] > INT32_MAX - tiles) {
-      const int rc = launch(b, mode, st);
+      const int rc = launch(b, mode, ctas_per_sm, st);
       if (rc != DFC_OK) return rc;
       reset();
     }
@@ -395,7 +404,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
     ++b.n_segs;
   }
-  return b.n_segs ? launch(b, mode, st) : DFC_OK;
+  return b.n_segs ? launch(b, mode, ctas_per_sm, st) : DFC_OK;
 }
 
 extern "C" int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64_t numel,

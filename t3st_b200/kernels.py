@@ -112,8 +112,10 @@ def unpack_moments(words: torch.Tensor, second: bool) -> None:
             _words(words).data_ptr(), words.numel(), int(second), _stream(dev)))
 
 
-def compress_ef(grad: torch.Tensor, comp: torch.Tensor, resid: torch.Tensor) -> None:
-    """bf16 compression with error feedback, in place on (comp, resid)."""
+def compress_ef(grad: torch.Tensor, comp: torch.Tensor, resid: torch.Tensor,
+                ctas_per_sm: int = 0) -> None:
+    """bf16 compression with error feedback, in place on (comp, resid);
+    ctas_per_sm > 0 caps the grid (room for a kernel beside it)."""
     dev = _need_cuda(grad, comp, resid)
     if grad.dtype != torch.float32:
         raise TypeError("grad must be FP32")
@@ -125,7 +127,8 @@ def compress_ef(grad: torch.Tensor, comp: torch.Tensor, resid: torch.Tensor) -> 
         raise ValueError("tensors must be contiguous")
     with torch.cuda.device(dev):
         _lib.check("dfc_compress_ef", _lib.lib().dfc_compress_ef(
-            grad.data_ptr(), comp.data_ptr(), resid.data_ptr(), grad.numel(), _stream(dev)))
+            grad.data_ptr(), comp.data_ptr(), resid.data_ptr(), grad.numel(), int(ctas_per_sm),
+            _stream(dev)))
 
 
 def grad_refs(grads: Sequence[torch.Tensor]) -> np.ndarray:

@@ -48,6 +48,14 @@ from .torch_fiber import _FORMATS, hyper_row
 PARAM_ALIGN = 16   # elements (64 bytes)
 PIECE_ALIGN = 64   # elements (256 bytes)
 DEFAULT_BUCKET = 1 << 26  # elements per bucket (256 MB of FP32 parameters)
+# Grid caps of the peer/nvls pipeline (see __init__): the fused kernel one
+# CTA per tile; the compression beside it 3 CTAs per SM at 2 ranks, 4 beyond
+# (sweep on B200 over 2^30 elements, ms per step at 2 ranks for caps
+# 2/3/4/5/6/uncapped: 6.18/5.53/5.69/6.00/6.21/6.51; at 4 ranks for 3/4/
+# uncapped: 7.72/7.43/8.78)
+FUSED_CTAS_PER_SM = 0
+COMPRESS_CTAS_PER_SM = {2: 3}
+COMPRESS_CTAS_DEFAULT = 4
 
 
 class CudaKernels:
@@ -57,9 +65,10 @@ class CudaKernels:
 
     def __init__(self):
         self._segs = {}
+        self.compress_ctas = 0  # CTAs per SM of the compression grid (0: the whole SM)
 
     def compress_ef(self, grad, comp, resid):
-        kernels.compress_ef(grad, comp, resid)
+        kernels.compress_ef(grad, comp, resid, self.compress_ctas)
 
     def step(self, segments, hyper_rows, hyper_index, mode, device, key=0):
         segs = self._segs.get(key)
@@ -91,9 +100,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     needs NVLink multicast;
                     "auto" (default): the measured fastest -- on B200 over a
                     2^30-element vector, ms per step (peer / nvls / nccl):
-                    2 ranks 6.5 / 10.0 / 10.5; 4 ranks - / 9.1 / 11.2;
-                    8 ranks 10.0 / 9.1 / 11.2.  So peer at 2 ranks, nvls
-                    from 4 on (nccl where the node has no multicast)
+                    2 ranks 5.5 / 9.1 / 10.5; 4 ranks 7.4 / 8.1 / 11.2;
+                    8 ranks 10.0 / 9.1 / 11.2 (before the compression cap).
+                    So peer up to 4 ranks, nvls beyond where the node has
+                    NVLink multicast, else peer
+    fused_ctas_per_sm, compress_ctas_per_sm
+                    grid caps of the peer/nvls pipeline (defaults measured)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -102,7 +114,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  moment_format: str = "packed", process_group=None,
                  compress_grads: bool | None = None, average_grads: bool = True,
                  bucket_elems: int = DEFAULT_BUCKET, transport: str = "auto",
-                 barrier_timeout_s: float = 30.0, backend=None):
+                 barrier_timeout_s: float = 30.0, backend=None,
+                 fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -126,20 +139,34 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         if self.transport in ("peer", "nvls") and not self.compress:
             raise ValueError("the peer and nvls transports reduce bf16 compressed gradients")
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
+        # Peer and nvls transports: the fused kernel of bucket b and the
+        # compression of bucket b+1 run on two streams.  The compression grid
+        # is capped so that the fused kernel finds room on every SM beside it;
+        # uncapped, its full-SM persistent grid makes the fused kernel wait,
+        # and the two run one after the other.  The fused kernel keeps one CTA
+        # per tile, so it takes the whole SM once the compression is done
+        # (a persistent fused grid of 2 or 3 CTAs per SM measured slower).
+        fk = FUSED_CTAS_PER_SM
+        ck = COMPRESS_CTAS_PER_SM.get(self.world, COMPRESS_CTAS_DEFAULT)
+        self.fused_ctas = fk if fused_ctas_per_sm is None else int(fused_ctas_per_sm)
+        compress_ctas = ck if compress_ctas_per_sm is None else int(compress_ctas_per_sm)
+        if self.transport in ("peer", "nvls") and isinstance(self.kernels, CudaKernels):
+            self.kernels.compress_ctas = compress_ctas
         self._layout(bucket_elems)
         if self.transport in ("peer", "nvls"):
             self._setup_peer()
 
     def _auto_transport(self, backend) -> str:
         """The measured fastest on B200 over a 2^30-element vector: the
-        peer-memory kernel at 2 ranks; the NVSwitch-multicast kernel from 4
-        ranks on where the node has NVLink multicast; NCCL otherwise (or for
-        uncompressed gradients, a custom backend or non-CUDA parameters)."""
+        peer-memory kernel up to 4 ranks; beyond, the NVSwitch-multicast
+        kernel where the node has NVLink multicast, else the peer kernel;
+        NCCL for one rank, uncompressed gradients, a custom backend or
+        non-CUDA parameters."""
         params = [p for g in self.param_groups for p in g["params"]]
         if self.world < 2 or not self.compress or backend is not None or \
                 not all(p.is_cuda for p in params):
             return "nccl"
-        if self.world == 2:
+        if self.world <= 4:
             return "peer"
         from torch._C._autograd import DeviceType
         from torch._C._distributed_c10d import _SymmetricMemory
@@ -149,7 +176,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                                                                params[0].device.index)
         except RuntimeError:  # no CUDA driver to ask
             multicast = False
-        return "nvls" if multicast else "nccl"
+        return "nvls" if multicast else "peer"
 
     # ---- layout -----------------------------------------------------------
     @torch.no_grad()
@@ -306,7 +333,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     _lib.check("dfc_zero_fused_step", lib.dfc_zero_fused_step(
                         _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self._comp_mc,
                         self._param_mc, self.world, self.rank, _lib.ptr(segs), len(segs),
-                        _lib.ptr(hyp), len(rows), self.mode, None, side.cuda_stream))
+                        _lib.ptr(hyp), len(rows), self.mode, None, self.fused_ctas,
+                        side.cuda_stream))
             self._barrier(side.cuda_stream)
         main.wait_stream(side)
 

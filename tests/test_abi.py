@@ -86,11 +86,11 @@ def test_step_rejects_bad_arguments_before_launch():
 
 def test_other_entry_points_reject_bad_arguments():
     lib = _lib.lib()
-    assert lib.dfc_compress_ef(None, None, None, -1, None) == _lib.DFC_ERR_SIZE
-    assert lib.dfc_compress_ef(None, None, None, 0, None) == _lib.DFC_OK
-    assert lib.dfc_compress_ef(None, 0x1000, 0x2000, 4, None) == _lib.DFC_ERR_NULL
-    assert lib.dfc_compress_ef(0x1002, 0x1000, 0x2000, 4, None) == _lib.DFC_ERR_ALIGN
-    assert lib.dfc_compress_ef(0x1000, 0x1001, 0x2000, 4, None) == _lib.DFC_ERR_ALIGN
+    assert lib.dfc_compress_ef(None, None, None, -1, 0, None) == _lib.DFC_ERR_SIZE
+    assert lib.dfc_compress_ef(None, None, None, 0, 0, None) == _lib.DFC_OK
+    assert lib.dfc_compress_ef(None, 0x1000, 0x2000, 4, 0, None) == _lib.DFC_ERR_NULL
+    assert lib.dfc_compress_ef(0x1002, 0x1000, 0x2000, 4, 0, None) == _lib.DFC_ERR_ALIGN
+    assert lib.dfc_compress_ef(0x1000, 0x1001, 0x2000, 4, 0, None) == _lib.DFC_ERR_ALIGN
     assert lib.dfc_pack_moments(None, -1, 0, None) == _lib.DFC_ERR_SIZE
     assert lib.dfc_pack_moments(None, 4, 0, None) == _lib.DFC_ERR_NULL
     assert lib.dfc_unpack_moments(0x1001, 4, 1, None) == _lib.DFC_ERR_ALIGN

@@ -16,6 +16,9 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(257, 31), (31,), (4099,), (3, 3, 3), (1 << 16,)]
+# a piece of ~1M elements per rank at two ranks: 513 tiles of 2048, so with
+# one fused CTA per SM each CTA walks several tiles
+SHAPES_LARGE = [(1 << 21,), (3001,), (257, 31)]
 
 
 def _grads(rank, step, sizes):
@@ -45,15 +48,17 @@ def _check_switch_sums(opt, red, world):
     assert bad.size == 0, (bad[:8], got[bad[:8]], exact[bad[:8]])
 
 
-def _run(rank, world, device, compress, transport="nccl"):
+def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=8192,
+         fused_ctas=None):
     from t3st_b200.zero import ShardedDFCAdamW
 
     torch.manual_seed(0)
-    params = [torch.nn.Parameter((torch.randn(s) * 0.02).to(device)) for s in SHAPES]
+    params = [torch.nn.Parameter((torch.randn(s) * 0.02).to(device)) for s in shapes]
     sizes = [p.numel() for p in params]
     p0 = [p.detach().cpu().numpy().reshape(-1).copy() for p in params]
     opt = ShardedDFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed",
-                          compress_grads=compress, bucket_elems=8192, transport=transport)
+                          compress_grads=compress, bucket_elems=bucket, transport=transport,
+                          fused_ctas_per_sm=fused_ctas)
     sim_p = [x.copy() for x in p0]
     sim_m = [np.zeros(n, np.uint32) for n in sizes]
     sim_v = [np.zeros(n, np.uint32) for n in sizes]
@@ -121,7 +126,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, transport, q):
+def _worker(rank, world, port, transport, q, kw):
     try:
         import datetime
 
@@ -134,7 +139,7 @@ def _worker(rank, world, port, transport, q):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
-        _run(rank, world, dev, True, transport)
+        _run(rank, world, dev, True, transport, **kw)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
@@ -149,13 +154,14 @@ def _multicast_ok() -> bool:
     return _SymmetricMemory.has_multicast_support(DeviceType.CUDA, 0)
 
 
-def _spawn(world, transport):
+def _spawn(world, transport, **kw):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, transport, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, transport, q, kw))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(world))
@@ -172,6 +178,17 @@ def test_sharded_on_two_gpus(transport):
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
     _spawn(2, transport)
+
+
+@pytest.mark.parametrize("transport", ["peer", "nvls"])
+def test_fused_kernel_walks_tiles_on_two_gpus(transport):
+    """One fused CTA per SM over a ~1M-element piece: every CTA of the
+    persistent grid steps several tiles; bit-exact as above."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if transport == "nvls" and not _multicast_ok():
+        pytest.skip("no NVLink multicast on this node")
+    _spawn(2, transport, shapes=SHAPES_LARGE, bucket=1 << 22, fused_ctas=1)
 
 
 @pytest.mark.parametrize("world", [4, 8])

@@ -212,9 +212,9 @@ def test_lost_rank_surfaces_as_error_not_hang():
 
 def test_auto_transport_choice():
     """The automatic transport: NCCL for one rank, uncompressed gradients,
-    a custom backend or CPU tensors; the peer kernel at 2 ranks; the
-    multicast kernel from 4 ranks only where the node reports NVLink
-    multicast (never on a machine without a CUDA driver)."""
+    a custom backend or CPU tensors; the peer kernel up to 4 ranks; beyond,
+    the multicast kernel only where the node reports NVLink multicast (never
+    on a machine without a CUDA driver), else the peer kernel."""
     import types
 
     from t3st_b200.zero import ShardedDFCAdamW
@@ -231,8 +231,9 @@ def test_auto_transport_choice():
 
     assert choose(1) == "nccl"
     assert choose(2) == "peer"
+    assert choose(4) == "peer"
     assert choose(2, compress=False) == "nccl"
     assert choose(2, backend=object()) == "nccl"
     assert choose(4, cuda=False) == "nccl"
     if not torch.cuda.is_available():
-        assert choose(8) == "nccl"
+        assert choose(8) == "peer"
