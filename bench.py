@@ -9,9 +9,12 @@ params N(0,0.02), grads N(0,1e-3), packed moments (bf16 high half + 16-bit
 error-feedback residual) warmed for 10 steps, one fused launch per step
 through DFCAdamW.step().
 N>1 (under torchrun) -- ZeRO-1 sharded step over a flat 2^30-element FP32
-parameter vector: bf16 compressed gradients with error feedback, NCCL
-reduce-scatter, fused packed step on the rank's 1/N shard, FP32 all-gather
-of the params (strong scaling: the vector is fixed, ranks split its state).
+parameter vector: bf16 compressed gradients with error feedback, reduction
+of the bf16 gradients, fused packed step on the rank's 1/N shard, FP32
+parameter broadcast (strong scaling: the vector is fixed, ranks split its
+state).  --transport auto picks the measured fastest: one fused kernel over
+NVLink peer memory up to 4 ranks, the same kernel through NVSwitch
+multicast beyond; nccl (reduce-scatter + step + all-gather) on request.
 
 Prints one JSON line on rank 0.  Timing: W untimed steps, then K steps
 between barrier + synchronize, CUDA events on the launching stream, max over
@@ -661,13 +664,21 @@ def run_sharded(args, rank, world, device):
     ms = max_over_ranks(e0.elapsed_time(e1), world, device)
     clocks = sampler.stop() if sampler is not None else {"skipped": "rank > 0 or --no-clocks"}
     value = P * K / (ms / 1e3)
-    # roofline: the slower of this rank's HBM bytes and its NVLink bytes
-    hbm_bytes = 12 * P + 26 * P // world          # compress over P, step over the shard
+    # roofline: the slower of the bytes through this rank's HBM and its NVLink
+    # bytes.  HBM counts the peers' traffic into this GPU's memory too.
     if opt.transport == "nvls":
+        # compress over P; own step reads p, m, v and writes m, v (20 B/elem of
+        # the shard); the switch reads all of this rank's bf16 gradients (2P)
+        # and writes every rank's FP32 parameters here (4P)
+        hbm_bytes = 12 * P + 20 * P // world + 6 * P
         # in: the reduced bf16 piece + every rank's FP32 parameters (own included,
         # through the switch); out: all bf16 gradients + the FP32 piece once
         nvl_bytes = max(2 * P // world + 4 * P, 2 * P + 4 * P // world)
     else:
+        # compress over P; step over the shard (26 B/elem: bf16 gradient, p, m,
+        # v, p written); the peers' reads of this rank's bf16 gradients for
+        # their pieces and their FP32 parameter writes here: 6 B/elem of the rest
+        hbm_bytes = 12 * P + 26 * P // world + 6 * P * (world - 1) // world
         nvl_bytes = 6 * P * (world - 1) // world  # bf16 RS + FP32 AG, per direction
     peak, peak_kind = measured_hbm_peak()
     t_hbm = hbm_bytes / (peak * 1e9)

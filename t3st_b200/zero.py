@@ -101,9 +101,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     "auto" (default): the measured fastest -- on B200 over a
                     2^30-element vector, ms per step (peer / nvls / nccl):
                     2 ranks 5.5 / 9.1 / 10.5; 4 ranks 7.4 / 8.1 / 11.2;
-                    8 ranks 10.0 / 9.1 / 11.2 (before the compression cap).
-                    So peer up to 4 ranks, nvls beyond where the node has
-                    NVLink multicast, else peer
+                    8 ranks 9.0 / 8.0 / 11.2.  So peer up to 4 ranks, nvls
+                    beyond where the node has NVLink multicast, else peer
     fused_ctas_per_sm, compress_ctas_per_sm
                     grid caps of the peer/nvls pipeline (defaults measured)
     """
