@@ -67,6 +67,8 @@ def parse_args():
                     help="measure only the replay-record codec (one GPU) and print its JSON")
     ap.add_argument("--replay-batch", type=int, default=65536,
                     help="records per codec launch")
+    ap.add_argument("--no-sharded-1gpu", action="store_true",
+                    help="N=1: skip the one-GPU run of the sharded compressed-gradient step")
     ap.add_argument("--no-host-overhead", action="store_true",
                     help="skip the host-overhead measurement (profiling runs)")
     ap.add_argument("--transport", choices=("auto", "peer", "nvls", "nccl"), default="auto",
@@ -439,6 +441,8 @@ def run_single(args, device):
     }
 
     line["reference_default_format"] = run_fp32_format(args, device, peak)
+    if not args.no_sharded_1gpu:
+        line["sharded_1gpu"] = run_sharded_1gpu(device, peak, peak_kind)
     if not args.no_host_overhead:
         line["host_us_per_step"] = host_overhead_us(opt)
     if not args.no_e2e:
@@ -550,6 +554,60 @@ def run_fp32_format(args, device, peak, K=300):
             "unit": UNIT, "ms_per_step": ms, "steps": K, "hbm_gbs": gbs,
             "frac_of_measured_hbm": gbs / peak,
             "kernel": "dfc::step_kernel<SIGNFIBER> (6 CTAs/SM)"}
+
+
+def run_sharded_1gpu(device, peak, peak_kind, K=30):
+    """The N>1 workload on one GPU: ShardedDFCAdamW over the flat 2^30-element
+    vector with bf16 error-feedback compression (no collective at one rank):
+    compression over P, then the packed step reading the bf16 gradients.
+    The one-GPU point of the sharded compressed-gradient step's 1..8 series."""
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    P = ZERO_PARAMS
+    gen = torch.Generator(device=device).manual_seed(1234)
+    param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
+    opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
+                          moment_format="packed", compress_grads=True)
+    del param
+    opt.flat_grad[:P].normal_(0.0, 1e-3, generator=gen)
+    for _ in range(3):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    hbm_bytes = 12 * P + 26 * P  # compression over P, step over P with bf16 gradients
+    gbs = hbm_bytes / (ms / 1e3) / 1e9
+    # the compression kernel alone over the whole vector (one launch, 12 B/elem)
+    from t3st_b200 import kernels
+
+    Kc = 10
+    e0.record(stream)
+    for _ in range(Kc):
+        kernels.compress_ef(opt.flat_grad[:P], opt.comp[:P], opt.resid[:P])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    c_ms = e0.elapsed_time(e1) / Kc
+    c_gbs = 12 * P / (c_ms / 1e3) / 1e9
+    out = {"workload": "ShardedDFCAdamW at one rank over the flat 2^30-element FP32 vector: "
+                       "bf16 error-feedback compression + packed step (bf16 gradients)",
+           "params": P, "steps": K, "ms_per_step": ms, "value": P / (ms / 1e3), "unit": UNIT,
+           "gpu_launches_per_step": 2 * opt.n_buckets,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                        "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                        "algorithmic_bytes_per_param": 38},
+           "compress_kernel": {"ms_per_launch": c_ms, "elements": P, "launches": Kc,
+                               "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak,
+                                            "unit": "GB/s", "frac": c_gbs / peak,
+                                            "algorithmic_bytes_per_elem": 12}}}
+    del opt
+    torch.cuda.empty_cache()
+    return out
 
 
 def cpu_model() -> str:

@@ -23,22 +23,51 @@ __device__ __forceinline__ void compress1(float g, uint32_t& c, uint32_t& q) {
   q = w & 0xFFFFu;
 }
 
+// Four elements (one float4 of g, one 8-byte word each of comp and resid)
+// per quad; bits of lane u in the 16-bit halves of the words.
+__device__ __forceinline__ void compress_quad(const float4& G, uint2& C, uint2& Q) {
+  uint32_t c0 = C.x & 0xFFFFu, c1 = C.x >> 16, c2 = C.y & 0xFFFFu, c3 = C.y >> 16;
+  uint32_t q0 = Q.x & 0xFFFFu, q1 = Q.x >> 16, q2 = Q.y & 0xFFFFu, q3 = Q.y >> 16;
+  compress1(G.x, c0, q0);
+  compress1(G.y, c1, q1);
+  compress1(G.z, c2, q2);
+  compress1(G.w, c3, q3);
+  C = make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
+  Q = make_uint2(q0 | (q1 << 16), q2 | (q3 << 16));
+}
+
+// Grid-stride over quads, two quads (a grid stride apart) per thread per
+// iteration: both quads' loads are issued before either is used, so a
+// capped grid (a few CTAs per SM) still keeps enough bytes in flight.  Each
+// warp-wide access covers 32 consecutive quads.
 __global__ void __launch_bounds__(kThreads)
     compress_vec_kernel(const float* __restrict__ g, uint16_t* __restrict__ comp,
                         uint16_t* __restrict__ resid, int64_t n4) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; j < n4; j += stride) {
-    const float4 G = __ldcs(reinterpret_cast<const float4*>(g) + j);
-    uint2 C = __ldcs(reinterpret_cast<const uint2*>(comp) + j);
-    uint2 Q = __ldcs(reinterpret_cast<const uint2*>(resid) + j);
-    uint32_t c0 = C.x & 0xFFFFu, c1 = C.x >> 16, c2 = C.y & 0xFFFFu, c3 = C.y >> 16;
-    uint32_t q0 = Q.x & 0xFFFFu, q1 = Q.x >> 16, q2 = Q.y & 0xFFFFu, q3 = Q.y >> 16;
-    compress1(G.x, c0, q0);
-    compress1(G.y, c1, q1);
-    compress1(G.z, c2, q2);
-    compress1(G.w, c3, q3);
-    __stcs(reinterpret_cast<uint2*>(comp) + j, make_uint2(c0 | (c1 << 16), c2 | (c3 << 16)));
-    __stcs(reinterpret_cast<uint2*>(resid) + j, make_uint2(q0 | (q1 << 16), q2 | (q3 << 16)));
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  uint2* c2 = reinterpret_cast<uint2*>(comp);
+  uint2* q2 = reinterpret_cast<uint2*>(resid);
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; j < n4; j += 2 * stride) {
+    const int64_t k = j + stride;
+    const bool two = k < n4;
+    const float4 G0 = __ldcs(g4 + j);
+    uint2 C0 = __ldcs(c2 + j);
+    uint2 Q0 = __ldcs(q2 + j);
+    float4 G1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint2 C1 = make_uint2(0u, 0u), Q1 = make_uint2(0u, 0u);
+    if (two) {
+      G1 = __ldcs(g4 + k);
+      C1 = __ldcs(c2 + k);
+      Q1 = __ldcs(q2 + k);
+    }
+    compress_quad(G0, C0, Q0);
+    __stcs(c2 + j, C0);
+    __stcs(q2 + j, Q0);
+    if (two) {
+      compress_quad(G1, C1, Q1);
+      __stcs(c2 + k, C1);
+      __stcs(q2 + k, Q1);
+    }
   }
 }
 

@@ -215,7 +215,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         if self.compress:
             self.comp = self._alloc(self.padded, torch.int16)
             self.resid = torch.zeros(self.padded, dtype=torch.int16, device=dev)
-            self.shard_grad = torch.zeros(local, dtype=torch.bfloat16, device=dev)
+            # one rank: the step reads the compressed gradients where they are
+            self.shard_grad = self.comp.view(torch.bfloat16) if n == 1 else \
+                torch.zeros(local, dtype=torch.bfloat16, device=dev)
         elif n > 1:
             self.shard_grad = torch.zeros(local, dtype=torch.float32, device=dev)
         else:
@@ -417,8 +419,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             if self.compress:
                 self.kernels.compress_ef(self._bucket(self.flat_grad, b),
                                          self._bucket(self.comp, b), self._bucket(self.resid, b))
-                if n == 1:
-                    self._local(self.shard_grad, b).copy_(self._bucket(self.comp, b).view(torch.bfloat16))
+                if n == 1:  # shard_grad is comp itself
                     return None
                 src = self._bucket(self.comp, b).view(torch.bfloat16)
             elif n > 1:
