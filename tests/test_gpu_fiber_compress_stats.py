@@ -66,6 +66,27 @@ def test_compress_matches_oracle_over_steps(cuda, n, offset):
         np.testing.assert_array_equal(q.cpu().numpy().view(np.uint16), hq)
 
 
+@pytest.mark.parametrize("ctas_per_sm", [1, 3])
+def test_compress_capped_grid_matches_oracle(cuda, ctas_per_sm):
+    """The grid capped as the ZeRO-1 pipeline caps it: every thread walks
+    several grid strides, two quads per iteration (odd quad counts leave one
+    thread a single quad), plus a scalar tail."""
+    n = (1 << 21) + 4 * 129 + 3
+    rng = np.random.default_rng(ctas_per_sm)
+    g = torch.zeros(n, device=cuda)
+    c = torch.zeros(n, dtype=torch.int16, device=cuda)
+    q = torch.zeros(n, dtype=torch.int16, device=cuda)
+    hc = np.zeros(n, np.uint16)
+    hq = np.zeros(n, np.uint16)
+    for _ in range(3):
+        x = (rng.standard_t(3, n) * 1e-3).astype(np.float32)
+        g.copy_(torch.from_numpy(x))
+        kernels.compress_ef(g, c, q, ctas_per_sm)
+        O.compress_ef(x, hc, hq)
+        np.testing.assert_array_equal(c.cpu().numpy().view(np.uint16), hc)
+        np.testing.assert_array_equal(q.cpu().numpy().view(np.uint16), hq)
+
+
 def test_grad_stats_match_oracle(cuda):
     rng = np.random.default_rng(8)
     sizes = [0, 1, 5, 8192, 8193, 100003, 1 << 20]
