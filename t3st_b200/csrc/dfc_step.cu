@@ -185,12 +185,18 @@ template <int MODE, int GDT, int PDT, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, MODE == DFC_MODE_PACKED ? DFC_STEP_MIN_BLOCKS
                                                                   : DFC_STEP_MIN_BLOCKS_FP32)
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
+  // Programmatic dependent launch: the next step's grid may start once every
+  // CTA of this one has started, and waits (griddepcontrol.wait) for this
+  // grid to finish before it touches memory.  Without a programmatic
+  // predecessor the wait returns at once.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int32_t t = static_cast<int32_t>(blockIdx.x);
   int lo = 0, hi = b.n_segs;  // tile_base[lo] <= t < tile_base[hi]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // before the first global access
   const SegArg& sg = b.seg[lo];
   const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
   const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
@@ -201,18 +207,37 @@ __global__ void __launch_bounds__(kThreads, MODE == DFC_MODE_PACKED ? DFC_STEP_M
 // type combination code: gradient type | parameter type << 2
 int32_t types_of(const DfcSegment& s) { return s.grad_dtype | (s.param_dtype << 2); }
 
+// Launch with programmatic stream serialization allowed: when the previous
+// kernel on the stream is a step kernel (back-to-back optimizer steps), this
+// grid's CTAs become resident during its tail instead of after it.
+template <int MODE, int GDT, int PDT, int MAXS, int MAXH>
+cudaError_t launch_one(const StepBatch<MAXS, MAXH>& b, int32_t grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, step_kernel<MODE, GDT, PDT, MAXS, MAXH>, b);
+}
+
 template <int MODE, int MAXS, int MAXH>
-void launch_types(const StepBatch<MAXS, MAXH>& b, int32_t types, int32_t grid, cudaStream_t st) {
+cudaError_t launch_types(const StepBatch<MAXS, MAXH>& b, int32_t types, int32_t grid,
+                         cudaStream_t st) {
   switch (types) {
-    case 0: step_kernel<MODE, 0, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 1: step_kernel<MODE, 1, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 2: step_kernel<MODE, 2, 0, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 4: step_kernel<MODE, 0, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 5: step_kernel<MODE, 1, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 6: step_kernel<MODE, 2, 1, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 8: step_kernel<MODE, 0, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    case 9: step_kernel<MODE, 1, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
-    default: step_kernel<MODE, 2, 2, MAXS, MAXH><<<grid, kThreads, 0, st>>>(b); break;
+    case 0: return launch_one<MODE, 0, 0>(b, grid, st);
+    case 1: return launch_one<MODE, 1, 0>(b, grid, st);
+    case 2: return launch_one<MODE, 2, 0>(b, grid, st);
+    case 4: return launch_one<MODE, 0, 1>(b, grid, st);
+    case 5: return launch_one<MODE, 1, 1>(b, grid, st);
+    case 6: return launch_one<MODE, 2, 1>(b, grid, st);
+    case 8: return launch_one<MODE, 0, 2>(b, grid, st);
+    case 9: return launch_one<MODE, 1, 2>(b, grid, st);
+    default: return launch_one<MODE, 2, 2>(b, grid, st);
   }
 }
 
@@ -220,10 +245,16 @@ template <int MAXS, int MAXH>
 int launch_batch(StepBatch<MAXS, MAXH>& b, int32_t mode, int32_t types, cudaStream_t st) {
   const int32_t tiles = b.tile_base[b.n_segs];
   if (tiles == 0) return DFC_OK;
+  cudaError_t e;
   switch (mode) {
-    case DFC_MODE_PLAIN: launch_types<DFC_MODE_PLAIN>(b, types, tiles, st); break;
-    case DFC_MODE_SIGNFIBER: launch_types<DFC_MODE_SIGNFIBER>(b, types, tiles, st); break;
-    default: launch_types<DFC_MODE_PACKED>(b, types, tiles, st); break;
+    case DFC_MODE_PLAIN: e = launch_types<DFC_MODE_PLAIN>(b, types, tiles, st); break;
+    case DFC_MODE_SIGNFIBER: e = launch_types<DFC_MODE_SIGNFIBER>(b, types, tiles, st); break;
+    default: e = launch_types<DFC_MODE_PACKED>(b, types, tiles, st); break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_cuda_error(e);
+    return DFC_ERR_CUDA;
   }
   return launch_status();
 }
