@@ -22,8 +22,10 @@ piece, sums them in FP32 in rank order, steps, and stores the new FP32
 parameters into every rank's copy; a cross-GPU barrier before it (every
 rank's C(b) done) and one at the end of the step (every rank's parameters
 done) order the ranks, and C(b+1) on the caller's stream overlaps the fused
-kernel of bucket b on a side stream.  Either way the step returns with the
-caller's stream ordered after all of it.
+kernel of bucket b on a side stream (the compression grid is capped so that
+the two kernels share the SMs).  transport="nvls" is the same kernel with
+the reduction and the broadcast done by the NVSwitch.  Either way the step
+returns with the caller's stream ordered after all of it.
 
 The parameters are re-homed into one flat FP32 buffer (each becomes a view
 of it) and their ``.grad`` into one flat gradient buffer, so the collectives
