@@ -20,6 +20,8 @@ from __future__ import annotations
 
 import math
 import operator
+from collections import deque
+from itertools import repeat
 from typing import Iterable
 
 import numpy as np
@@ -318,6 +320,7 @@ class DFCAdamW(torch.optim.Optimizer):
 _GRAD = operator.attrgetter("grad")
 _DTYPE = operator.attrgetter("dtype")
 _STEP = operator.itemgetter("step")
+_IS_SPARSE = operator.attrgetter("is_sparse")
 _DATA_PTR = torch.Tensor.data_ptr
 _STRIDE = torch.Tensor.stride
 
@@ -343,6 +346,8 @@ class _FastPlan:
         self.segs["hyper"] = [w[3] for w in work]
         self.hyp = np.zeros(len(opt.param_groups), dtype=_lib.HYPER_DTYPE)
         self.n_groups = len(opt.param_groups)
+        self.segs_ptr = _lib.ptr(self.segs)  # both arrays live as long as the plan
+        self.hyp_ptr = _lib.ptr(self.hyp)
 
     def try_step(self, opt: "DFCAdamW") -> bool:
         grads = list(map(_GRAD, self.params))
@@ -350,14 +355,22 @@ class _FastPlan:
             gptrs = list(map(_DATA_PTR, grads))
         except TypeError:  # a parameter without gradient
             return False
-        if gptrs != self.gptrs or list(map(_DATA_PTR, self.params)) != self.pptrs:
+        if list(map(_DATA_PTR, self.params)) != self.pptrs:
             return False
         if not all(map(operator.is_, grads, self.grads)):
+            # new gradient tensors (zero_grad(set_to_none=True) then backward):
+            # PyTorch keeps a .grad on its parameter's device with its shape and
+            # dtype; the plan holds while the layout matches, with new pointers
             if (list(map(_DTYPE, grads)) != self.gdtypes
                     or list(map(_STRIDE, grads)) != self.gstrides
-                    or any(map(operator.attrgetter("is_sparse"), grads))):
+                    or any(map(_IS_SPARSE, grads))):
                 return False
+            if gptrs != self.gptrs:
+                self.segs["grad"] = gptrs
+                self.gptrs = gptrs
             self.grads = grads
+        elif gptrs != self.gptrs:  # storage swapped under the same tensor
+            return False
         steps = list(map(_STEP, self.states))
         s = steps[0]
         if steps.count(s) != len(steps) or opt.mode != self.mode or \
@@ -380,10 +393,9 @@ class _FastPlan:
         if opt.max_grad_norm is not None:
             scale_ptr = opt._clip_scale(self.segs, dev, stream)
         _lib.check("dfc_mt_step", lib.dfc_mt_step(
-            _lib.ptr(self.segs), len(self.segs), _lib.ptr(self.hyp), self.n_groups, self.mode,
-            scale_ptr, stream))
-        for st in self.states:
-            st["step"] = s
+            self.segs_ptr, len(self.segs), self.hyp_ptr, self.n_groups, self.mode, scale_ptr,
+            stream))
+        deque(map(operator.setitem, self.states, repeat("step"), repeat(s)), 0)
         return True
 
 
