@@ -76,6 +76,8 @@ def parse_args():
                          "NVSwitch multicast, NCCL collectives, or the measured fastest for N")
     ap.add_argument("--fused-ctas", type=int, default=None,
                     help="N>1 peer/nvls: CTAs per SM of the fused kernel (0: one per tile)")
+    ap.add_argument("--bucket-elems", type=int, default=None,
+                    help="N>1: elements per pipelined bucket (default: ShardedDFCAdamW's)")
     ap.add_argument("--compress-ctas", type=int, default=None,
                     help="N>1 peer/nvls: CTAs per SM of the compression beside it (0: 8)")
     return ap.parse_args()
@@ -699,7 +701,9 @@ def run_sharded(args, rank, world, device):
     opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
                           moment_format="packed", transport=args.transport,
                           fused_ctas_per_sm=args.fused_ctas,
-                          compress_ctas_per_sm=args.compress_ctas)
+                          compress_ctas_per_sm=args.compress_ctas,
+                          **({} if args.bucket_elems is None else
+                             {"bucket_elems": args.bucket_elems}))
     del param
     ggen = torch.Generator(device=device).manual_seed(100 + rank)  # per-rank gradients
     opt.flat_grad[:P].normal_(0.0, 1e-3, generator=ggen)
@@ -759,6 +763,7 @@ def run_sharded(args, rank, world, device):
                 "params": P, "moment_format": "packed", "parallelism": f"zero1-dp{world}",
                 "transport": opt.transport,
                 "fused_ctas_per_sm": opt.fused_ctas,
+                "bucket_elems": opt.bucket, "buckets": opt.n_buckets,
                 "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
             },
