@@ -558,6 +558,53 @@ def run_fp32_format(args, device, peak, K=300):
             "kernel": "dfc::step_kernel<SIGNFIBER> (6 CTAs/SM)"}
 
 
+def run_fiber_kernels(words, device, peak, K):
+    """Sign-fiber payload I/O (dfc_fiber_write / dfc_fiber_read, C ABI) over
+    one range of second-moment words: bit 31 of each word is one payload
+    bit.  A write reads and rewrites each word and reads the packed byte
+    (8.125 B per bit); a read reads each word and writes the byte (4.125 B).
+    CUDA events over K calls each; the payload must read back unchanged."""
+    from t3st_b200 import _lib
+
+    lib = _lib.lib()
+    nbits = words.numel()
+    nbytes = nbits // 8
+    ranges = np.zeros(1, dtype=_lib.WORDRANGE_DTYPE)
+    ranges[0] = (words.data_ptr(), nbits)
+    payload = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=device,
+                            generator=torch.Generator(device=device).manual_seed(5))
+    back = torch.empty_like(payload)
+    stream = torch.cuda.current_stream(device)
+
+    def write():
+        _lib.check("dfc_fiber_write", lib.dfc_fiber_write(
+            _lib.ptr(ranges), 1, 0, nbytes * 8, payload.data_ptr(), stream.cuda_stream))
+
+    def read():
+        _lib.check("dfc_fiber_read", lib.dfc_fiber_read(
+            _lib.ptr(ranges), 1, 0, nbytes * 8, back.data_ptr(), stream.cuda_stream))
+
+    write()
+    read()
+    torch.cuda.synchronize()
+    if not torch.equal(back, payload):
+        raise RuntimeError("fiber bench: payload did not read back")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {"bits": nbytes * 8, "calls": K}
+    for name, fn, per_bit in (("write", write, 8.125), ("read", read, 4.125)):
+        e0.record(stream)
+        for _ in range(K):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / K
+        gbs = nbytes * 8 * per_bit / (ms / 1e3) / 1e9
+        out[name] = {"ms_per_call": ms, "bits_per_s": nbytes * 8 / (ms / 1e3),
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                  "frac": gbs / peak, "algorithmic_bytes_per_bit": per_bit}}
+    return out
+
+
 def run_sharded_1gpu(device, peak, peak_kind, K=30):
     """The N>1 workload on one GPU: ShardedDFCAdamW over the flat 2^30-element
     vector with bf16 error-feedback compression (no collective at one rank):
@@ -596,6 +643,16 @@ def run_sharded_1gpu(device, peak, peak_kind, K=30):
     torch.cuda.synchronize()
     c_ms = e0.elapsed_time(e1) / Kc
     c_gbs = 12 * P / (c_ms / 1e3) / 1e9
+    # per-buffer gradient statistics (sum of squares, max, non-finite count)
+    # over the FP32 gradient: 4 B/elem read, two passes (tiles, then records)
+    e0.record(stream)
+    for _ in range(Kc):
+        kernels.grad_stats([opt.flat_grad[:P]])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    s_ms = e0.elapsed_time(e1) / Kc
+    s_gbs = 4 * P / (s_ms / 1e3) / 1e9
+    fiber = run_fiber_kernels(opt.exp_avg_sq, device, peak, Kc)
     out = {"workload": "ShardedDFCAdamW at one rank over the flat 2^30-element FP32 vector: "
                        "bf16 error-feedback compression + packed step (bf16 gradients)",
            "params": P, "steps": K, "ms_per_step": ms, "value": P / (ms / 1e3), "unit": UNIT,
@@ -606,7 +663,12 @@ def run_sharded_1gpu(device, peak, peak_kind, K=30):
            "compress_kernel": {"ms_per_launch": c_ms, "elements": P, "launches": Kc,
                                "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak,
                                             "unit": "GB/s", "frac": c_gbs / peak,
-                                            "algorithmic_bytes_per_elem": 12}}}
+                                            "algorithmic_bytes_per_elem": 12}},
+           "grad_stats_kernels": {"ms_per_call": s_ms, "elements": P, "calls": Kc,
+                                  "roofline": {"bound": "hbm", "achieved": s_gbs, "peak": peak,
+                                               "unit": "GB/s", "frac": s_gbs / peak,
+                                               "algorithmic_bytes_per_elem": 4}},
+           "fiber_kernels": fiber}
     del opt
     torch.cuda.empty_cache()
     return out

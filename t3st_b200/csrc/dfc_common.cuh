@@ -15,6 +15,20 @@ void set_cuda_error(cudaError_t e);
 // Number of SMs of the current device (read once per device, then cached).
 int sm_count();
 
+// CTAs of `kernel` (threads per CTA, no dynamic shared memory) that are
+// resident at once on the current device: the largest grid a grid-stride
+// kernel should get, so that no CTA waits for a second wave.
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int threads) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return sm_count() * per_sm;
+}
+
 // Check for a launch error after queueing kernels.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -87,10 +87,13 @@ __global__ void __launch_bounds__(kThreads)
 // ctas_per_sm CTAs per SM (8, the whole SM at 256 threads, by default);
 // fewer for small buffers.  A smaller figure leaves room on every SM for a
 // kernel that runs beside this one (the ZeRO-1 fused step).
-int grid_for(int64_t work, int32_t ctas_per_sm) {
+// (never more than are resident at once: a grid-stride CTA that waits for a
+// second wave would finish its share late).
+template <typename Kernel>
+int grid_for(Kernel kernel, int64_t work, int32_t ctas_per_sm) {
   const int64_t per_sm = ctas_per_sm > 0 ? std::min(ctas_per_sm, 8) : 8;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + kThreads - 1) / kThreads,
-                                                                  sm_count() * per_sm)));
+  const int64_t cap = std::min<int64_t>(sm_count() * per_sm, resident_ctas(kernel, kThreads));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + kThreads - 1) / kThreads, cap)));
 }
 
 }  // namespace
@@ -107,10 +110,10 @@ extern "C" int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resi
   int64_t done = 0;
   if (aligned(grad, 16) && aligned(comp, 8) && aligned(resid, 8)) {
     const int64_t n4 = n / 4;
-    if (n4 > 0) compress_vec_kernel<<<grid_for(n4, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, n4);
+    if (n4 > 0) compress_vec_kernel<<<grid_for(compress_vec_kernel, n4, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, n4);
     done = n4 * 4;
   }
   if (done < n)
-    compress_scalar_kernel<<<grid_for(n - done, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, done, n);
+    compress_scalar_kernel<<<grid_for(compress_scalar_kernel, n - done, ctas_per_sm), kThreads, 0, st>>>(grad, comp, resid, done, n);
   return launch_status();
 }

@@ -1,10 +1,14 @@
 // Sign-fiber payload I/O on the device: bit 31 of every second-moment word,
 // concatenated over a list of word ranges, read into or written from a
-// little-endian packed byte buffer (remote/torch_fiber.py:120-185).  One
-// thread per payload byte; it owns the 8 words behind that byte, so writes
-// never race and a read is one pass.  The range list lives in launch
-// parameters (up to kMaxRanges per launch); a call with more ranges is split
-// into launches at byte boundaries of the payload.
+// little-endian packed byte buffer (remote/torch_fiber.py:120-185).  One lane
+// per word, so a warp's word accesses are coalesced: a read gathers the 32
+// lanes' bits with __ballot_sync into 4 payload bytes (bit j of the mask is
+// lane j's bit, which is the little-endian bit order of the payload); a
+// write reads its bit from the payload byte and rewrites its own word, so
+// writes never race.  Each warp takes kGroups groups of 32 words per
+// iteration, with every group's word load issued before the first use.  The
+// range list lives in launch parameters (up to kMaxRanges per launch); a call
+// with more ranges is split into launches at byte boundaries of the payload.
 #include <algorithm>
 
 #include "dfc_common.cuh"
@@ -34,28 +38,48 @@ __device__ __forceinline__ int find_range(const FiberBatch& b, int64_t g) {
   return lo;
 }
 
+constexpr int kGroups = 8;  // 32-word groups per warp per iteration
+
 template <bool WRITE>
 __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__ FiberBatch b,
                                                          uint8_t* bytes) {
+  const int lane = threadIdx.x & 31;
   const int64_t nbytes = (b.n_bits + 7) / 8;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t k = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; k < nbytes;
-       k += stride) {
-    const int nb = static_cast<int>(min(static_cast<int64_t>(8), b.n_bits - 8 * k));
-    int64_t g = b.first_bit + 8 * k;
-    int r = find_range(b, g);
-    uint32_t in = WRITE ? bytes[k] : 0u;
-    uint32_t out = 0u;
-    for (int j = 0; j < nb; ++j, ++g) {
-      while (g >= b.range_base[r + 1]) ++r;
-      uint32_t* w = b.words[r] + (g - b.range_base[r]);
-      if (WRITE) {
-        *w = (*w & 0x7FFFFFFFu) | (((in >> j) & 1u) << 31);
-      } else {
-        out |= (*w >> 31) << j;
+  const int64_t span = 32 * kGroups;  // payload bits per warp iteration
+  const int64_t n_iter = (b.n_bits + span - 1) / span;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+       w < n_iter; w += warps) {
+    const int64_t k0 = span * w;  // first payload bit of this iteration (warp-uniform)
+    int r = find_range(b, b.first_bit + k0);
+    uint32_t* ptr[kGroups];
+    uint32_t word[kGroups];
+#pragma unroll
+    for (int j = 0; j < kGroups; ++j) {
+      const int64_t k = k0 + 32 * j + lane;
+      ptr[j] = nullptr;
+      if (k < b.n_bits) {
+        const int64_t g = b.first_bit + k;
+        while (g >= b.range_base[r + 1]) ++r;  // ranges ascend with g
+        ptr[j] = b.words[r] + (g - b.range_base[r]);
       }
     }
-    if (!WRITE) bytes[k] = static_cast<uint8_t>(out);
+#pragma unroll
+    for (int j = 0; j < kGroups; ++j) word[j] = ptr[j] ? *ptr[j] : 0u;
+#pragma unroll
+    for (int j = 0; j < kGroups; ++j) {
+      const int64_t k = k0 + 32 * j + lane;
+      if (WRITE) {
+        if (ptr[j]) {
+          const uint32_t in = (static_cast<uint32_t>(bytes[k >> 3]) >> (k & 7)) & 1u;
+          *ptr[j] = (word[j] & 0x7FFFFFFFu) | (in << 31);
+        }
+      } else {
+        const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
+        const int64_t byte = (k0 + 32 * j) / 8 + lane;  // lanes 0..3: the group's 4 bytes
+        if (lane < 4 && byte < nbytes) bytes[byte] = static_cast<uint8_t>(mask >> (8 * lane));
+      }
+    }
   }
 }
 
@@ -109,8 +133,10 @@ int fiber_call(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit, 
       if (whole == 0) return DFC_ERR_SIZE;  // more than kMaxRanges ranges inside one byte
     }
     b.n_bits = end - first;
-    const int64_t nbytes = (b.n_bits + 7) / 8;
-    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nbytes + kThreads - 1) / kThreads, 148 * 8)));
+    const int64_t iters = (b.n_bits + 32 * kGroups - 1) / (32 * kGroups);  // warp iterations
+    const int64_t want = (iters + kThreads / 32 - 1) / (kThreads / 32);
+    const int grid = static_cast<int>(
+        std::max<int64_t>(1, std::min<int64_t>(want, resident_ctas(fiber_kernel<WRITE>, kThreads))));
     fiber_kernel<WRITE><<<grid, kThreads, 0, st>>>(b, bytes + done / 8);
     const int rc = launch_status();
     if (rc != DFC_OK) return rc;

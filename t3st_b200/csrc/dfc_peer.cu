@@ -414,7 +414,8 @@ extern "C" int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, in
   if (numel == 0) return DFC_OK;
   if (!comp_multicast || !out) return DFC_ERR_NULL;
   if (!aligned(comp_multicast, 16) || !aligned(out, 16)) return DFC_ERR_ALIGN;
-  const int64_t blocks = std::min<int64_t>((numel / kVec + kThreads - 1) / kThreads + 1, 148 * 8);
+  const int64_t blocks = std::min<int64_t>((numel / kVec + kThreads - 1) / kThreads + 1,
+                                           resident_ctas(multicast_sum_kernel, kThreads));
   multicast_sum_kernel<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(comp_multicast), out, numel);
   return launch_status();

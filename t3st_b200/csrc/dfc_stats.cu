@@ -1,11 +1,13 @@
 // Per-buffer gradient statistics (sum of squares, max |g|, non-finite count)
 // and the global-norm clip coefficient.
 //
-// Pass 1: one CTA per tile of kTile elements of one buffer; each thread
-// accumulates its elements (sum of squares in double), then the CTA reduces
-// with warp shuffles (__shfl_xor_sync butterfly) and one shared-memory step
-// across warps, and writes one partial record per tile to scratch.
-// Pass 2: one warp per buffer folds that buffer's partial records in a fixed
+// Pass 1: tiles of kTile elements of one buffer; a persistent grid (the CTAs
+// resident at once) walks them, each CTA prefetching its next tile while it
+// reduces the current one.  Per tile, each thread accumulates its elements
+// (sum of squares in double), the CTA reduces with warp shuffles
+// (__shfl_xor_sync butterfly) and one shared-memory step across warps, and
+// writes one partial record per tile to scratch.
+// Pass 2: one CTA per buffer folds that buffer's partial records in a fixed
 // order.  No atomics anywhere, so the result depends only on the input and
 // the tile size, never on scheduling.
 #include <algorithm>
@@ -74,36 +76,136 @@ __device__ __forceinline__ float load1(const BufArg& b, int64_t i) {
   return static_cast<const float*>(b.g)[i];
 }
 
-__global__ void __launch_bounds__(kThreads) stats_partial_kernel(const __grid_constant__ StatsBatch b) {
-  const int32_t t = static_cast<int32_t>(blockIdx.x);
+constexpr int kLoads = kTile / 4 / kThreads;  // float4 loads per thread in a full tile
+
+// Tile t's buffer (binary search over the tile prefix) and element range.
+struct TileRef {
+  const BufArg* buf;
+  int64_t base;
+  int64_t count;
+};
+
+__device__ __forceinline__ TileRef tile_ref(const StatsBatch& b, int32_t t) {
   int lo = 0, hi = b.n_bufs;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (b.tile_base[mid] <= t) lo = mid; else hi = mid;
   }
-  const BufArg& buf = b.buf[lo];
-  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
-  const int64_t count = min(static_cast<int64_t>(kTile), buf.n - base);
+  TileRef r;
+  r.buf = &b.buf[lo];
+  r.base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
+  r.count = min(static_cast<int64_t>(kTile), b.buf[lo].n - r.base);
+  return r;
+}
 
+__device__ __forceinline__ bool full_vec(const TileRef& r) { return r.buf->vec && r.count == kTile; }
+
+__device__ __forceinline__ void load_tile(const TileRef& r, float4 (&x)[kLoads]) {
+  const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(r.buf->g) + r.base);
+#pragma unroll
+  for (int u = 0; u < kLoads; ++u) x[u] = __ldcs(g4 + threadIdx.x + u * kThreads);
+}
+
+// This thread's share of one tile, in the order j = threadIdx.x, +kThreads, ...
+// (a full FP32 tile arrives preloaded in x).
+__device__ __forceinline__ Acc tile_acc(const TileRef& r, const float4 (&x)[kLoads], bool pre) {
   Acc acc{0.0, 0.0f, 0};
+  if (pre) {
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+      acc_add(acc, x[u].x);
+      acc_add(acc, x[u].y);
+      acc_add(acc, x[u].z);
+      acc_add(acc, x[u].w);
+    }
+    return acc;
+  }
+  const BufArg& buf = *r.buf;
   int64_t done = 0;
   if (buf.vec) {
-    const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(buf.g) + base);
-    const int64_t nv = count / 4;
+    const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(buf.g) + r.base);
+    const int64_t nv = r.count / 4;
     for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
-      const float4 x = __ldcs(g4 + j);
-      acc_add(acc, x.x);
-      acc_add(acc, x.y);
-      acc_add(acc, x.z);
-      acc_add(acc, x.w);
+      const float4 v = __ldcs(g4 + j);
+      acc_add(acc, v.x);
+      acc_add(acc, v.y);
+      acc_add(acc, v.z);
+      acc_add(acc, v.w);
     }
     done = nv * 4;
   }
-  for (int64_t j = done + threadIdx.x; j < count; j += kThreads) acc_add(acc, load1(buf, base + j));
+  for (int64_t j = done + threadIdx.x; j < r.count; j += kThreads) acc_add(acc, load1(buf, r.base + j));
+  return acc;
+}
 
+// Persistent: CTA c takes tiles c, c + gridDim.x, ...  A full FP32 tile's
+// loads are issued before the previous tile is reduced, so the SM keeps
+// loads in flight through the block reduction.  Each tile's record is the
+// same as with one CTA per tile: the per-thread order, the warp butterfly
+// and the fixed fold over warps do not depend on the grid.
+__global__ void __launch_bounds__(kThreads, 3) stats_partial_kernel(const __grid_constant__ StatsBatch b) {
+  __shared__ Acc part[2][kWarps];  // double-buffered: one barrier per tile
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t tiles = b.tile_base[b.n_bufs];
+  int32_t t = static_cast<int32_t>(blockIdx.x);
+  if (t >= tiles) return;
+  TileRef cur = tile_ref(b, t);
+  float4 x[kLoads];
+  bool pre = full_vec(cur);
+  if (pre) load_tile(cur, x);
+  for (int it = 0; t < tiles; t += static_cast<int32_t>(gridDim.x), ++it) {
+    Acc acc = tile_acc(cur, x, pre);
+    const int32_t tn = t + static_cast<int32_t>(gridDim.x);
+    TileRef nxt = cur;
+    bool pre_n = false;
+    if (tn < tiles) {
+      nxt = tile_ref(b, tn);
+      pre_n = full_vec(nxt);
+      if (pre_n) load_tile(nxt, x);  // x is free: this tile's values are in acc
+    }
+    acc = warp_fold(acc);
+    if (lane == 0) part[it & 1][warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      Acc tot = part[it & 1][0];
+      for (int w = 1; w < kWarps; ++w) acc_merge(tot, part[it & 1][w]);
+      DfcGradStats rec;
+      rec.sumsq = tot.s;
+      rec.amax = tot.a;
+      rec.reserved = 0;
+      rec.nonfinite = tot.bad;
+      b.partial[t] = rec;
+    }
+    cur = nxt;
+    pre = pre_n;
+  }
+}
+
+// One CTA per buffer folds that buffer's partial records: thread i takes
+// records i, i + kThreads, ... in order (loads batched kBatch at a time), then
+// the warp butterfly and a fixed fold over warps.  Deterministic.
+constexpr int kBatch = 4;
+
+__global__ void __launch_bounds__(kThreads) stats_final_kernel(const __grid_constant__ StatsBatch b) {
+  const int buf = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t t0 = b.tile_base[buf], t1 = b.tile_base[buf + 1];
+  Acc acc{0.0, 0.0f, 0};
+  for (int32_t t = t0 + threadIdx.x; t < t1; t += kBatch * kThreads) {
+    DfcGradStats r[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (t + u * kThreads < t1) r[u] = b.partial[t + u * kThreads];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (t + u * kThreads < t1) {
+        Acc o{r[u].sumsq, r[u].amax, r[u].nonfinite};
+        acc_merge(acc, o);
+      }
+    }
+  }
   acc = warp_fold(acc);
   __shared__ Acc part[kWarps];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) part[warp] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -114,29 +216,7 @@ __global__ void __launch_bounds__(kThreads) stats_partial_kernel(const __grid_co
     r.amax = tot.a;
     r.reserved = 0;
     r.nonfinite = tot.bad;
-    b.partial[t] = r;
-  }
-}
-
-__global__ void __launch_bounds__(kThreads) stats_final_kernel(const __grid_constant__ StatsBatch b) {
-  const int warp_global = (blockIdx.x * kThreads + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp_global >= b.n_bufs) return;
-  const int32_t t0 = b.tile_base[warp_global], t1 = b.tile_base[warp_global + 1];
-  Acc acc{0.0, 0.0f, 0};
-  for (int32_t t = t0 + lane; t < t1; t += 32) {
-    const DfcGradStats r = b.partial[t];
-    Acc o{r.sumsq, r.amax, r.nonfinite};
-    acc_merge(acc, o);
-  }
-  acc = warp_fold(acc);
-  if (lane == 0) {
-    DfcGradStats r;
-    r.sumsq = acc.s;
-    r.amax = acc.a;
-    r.reserved = 0;
-    r.nonfinite = acc.bad;
-    b.out[warp_global] = r;
+    b.out[buf] = r;
   }
 }
 
@@ -184,9 +264,9 @@ int grad_stats_launch(const DfcGradRef* grads, int32_t n_grads, DfcGradStats* ou
       ++i;
     }
     const int32_t tiles = b.tile_base[b.n_bufs];
-    stats_partial_kernel<<<tiles, kThreads, 0, st>>>(b);
-    const int warps_per_block = kThreads / 32;
-    stats_final_kernel<<<(b.n_bufs + warps_per_block - 1) / warps_per_block, kThreads, 0, st>>>(b);
+    const int32_t grid = static_cast<int32_t>(std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * 3));
+    stats_partial_kernel<<<grid, kThreads, 0, st>>>(b);
+    stats_final_kernel<<<b.n_bufs, kThreads, 0, st>>>(b);
     const int rc = launch_status();
     if (rc != DFC_OK) return rc;
     tile_off += tiles;

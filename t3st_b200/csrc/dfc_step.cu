@@ -368,11 +368,13 @@ int convert(uint32_t* w, int64_t n, bool pack, bool second, void* stream) {
   if (!w) return DFC_ERR_NULL;
   if (!aligned(w, 4)) return DFC_ERR_ALIGN;
   const int64_t want = (n + 255) / 256;
-  const int blocks = static_cast<int>(std::min<int64_t>(want, 148 * 16));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pack && second) convert_kernel<true, true><<<blocks, 256, 0, st>>>(w, n);
-  else if (pack) convert_kernel<true, false><<<blocks, 256, 0, st>>>(w, n);
-  else convert_kernel<false, false><<<blocks, 256, 0, st>>>(w, n);
+  auto grid = [&](auto kernel) {
+    return static_cast<int>(std::min<int64_t>(want, resident_ctas(kernel, 256)));
+  };
+  if (pack && second) convert_kernel<true, true><<<grid(convert_kernel<true, true>), 256, 0, st>>>(w, n);
+  else if (pack) convert_kernel<true, false><<<grid(convert_kernel<true, false>), 256, 0, st>>>(w, n);
+  else convert_kernel<false, false><<<grid(convert_kernel<false, false>), 256, 0, st>>>(w, n);
   return launch_status();
 }
 

@@ -114,6 +114,47 @@ def test_grad_stats_match_oracle(cuda):
     assert again.tobytes() == stats.tobytes()
 
 
+def test_grad_stats_large_buffers_match_oracle(cuda):
+    """Buffers of 1,101 and 611 tiles (8,192 elements each) with a ragged
+    tail: every CTA of the statistics pass walks several tiles (the next
+    tile's loads in flight during the block reduction), and the final fold
+    of the 1,101-tile buffer loops over batches of records."""
+    rng = np.random.default_rng(21)
+    xs = [(rng.standard_t(3, 8192 * 1100 + 5) * 1e-2).astype(np.float32),
+          (rng.standard_normal(8192 * 611) * 1e-3).astype(np.float32), np.ones(3, np.float32)]
+    xs[0][[17, 8192 * 700 + 1]] = [np.inf, -np.inf]
+    tg = [torch.from_numpy(x).to(cuda) for x in xs]
+    stats = kernels.stats_to_numpy(kernels.grad_stats(tg))
+    for i, x in enumerate(xs):
+        s, a, bad = O.grad_stats(x)
+        assert stats[i]["nonfinite"] == bad
+        assert stats[i]["amax"] == np.float32(a)
+        if np.isnan(s) or np.isinf(s):
+            assert stats[i]["sumsq"] == s or (np.isnan(s) and np.isnan(stats[i]["sumsq"]))
+        else:
+            assert stats[i]["sumsq"] == pytest.approx(s, rel=1e-12, abs=0)
+    again = kernels.stats_to_numpy(kernels.grad_stats(tg))
+    assert again.tobytes() == stats.tobytes()
+
+
+def test_fiber_large_ranges_round_trip(cuda):
+    """Ranges of millions of words: every warp of the fiber kernels walks
+    several groups of 256 words, including across range boundaries."""
+    rng = np.random.default_rng(22)
+    sizes = [3_000_001, 5, 2_500_000, 777_777]
+    params = [torch.nn.Parameter(torch.zeros(s, device=cuda)) for s in sizes]
+    opt = DFCAdamW(params)
+    ch = TorchSignFiberChannel(opt)
+    payload = rng.integers(0, 256, ch.byte_capacity, dtype=np.uint8)
+    ch.write_device(0, torch.from_numpy(payload).to(cuda))
+    bits = _fiber_bits(opt.second_moment_tensors())
+    np.testing.assert_array_equal(np.packbits(bits[:8 * payload.size], bitorder="little"), payload)
+    np.testing.assert_array_equal(ch.read_device(0, payload.size).cpu().numpy(), payload)
+    # an unaligned window that starts inside the first range and ends in the last
+    start, count = 3 * 8 + 1, ch.bit_capacity - 40
+    np.testing.assert_array_equal(ch.read_bits(start, count), bits[start:start + count])
+
+
 def test_clip_coef_and_clipped_step(cuda):
     torch.manual_seed(0)
     shapes = [(300, 77), (1000,), (5,)]
