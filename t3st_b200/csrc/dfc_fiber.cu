@@ -52,6 +52,29 @@ __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__
        w < n_iter; w += warps) {
     const int64_t k0 = span * w;  // first payload bit of this iteration (warp-uniform)
     int r = find_range(b, b.first_bit + k0);
+    if (k0 + span <= b.n_bits && b.first_bit + k0 + span <= b.range_base[r + 1]) {
+      // The whole iteration lies in range r (the common case): one base
+      // pointer, and word (32 j + lane) of it for group j -- no per-word
+      // index arithmetic.  k0 + 32 j is a multiple of 8, so lane's payload
+      // bit is bit (lane & 7) of byte (k0 + 32 j + lane) / 8.
+      uint32_t* base = b.words[r] + (b.first_bit + k0 - b.range_base[r]) + lane;
+      uint32_t word[kGroups];
+#pragma unroll
+      for (int j = 0; j < kGroups; ++j) word[j] = base[32 * j];
+#pragma unroll
+      for (int j = 0; j < kGroups; ++j) {
+        if (WRITE) {
+          const uint32_t in = (static_cast<uint32_t>(bytes[(k0 + 32 * j + lane) >> 3]) >> (lane & 7)) & 1u;
+          base[32 * j] = (word[j] & 0x7FFFFFFFu) | (in << 31);
+        } else {
+          const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
+          if (lane < 4) bytes[(k0 + 32 * j) / 8 + lane] = static_cast<uint8_t>(mask >> (8 * lane));
+        }
+      }
+      continue;
+    }
+    // An iteration at a range boundary or at the end of the payload: each
+    // lane finds its own range.
     uint32_t* ptr[kGroups];
     uint32_t word[kGroups];
 #pragma unroll
