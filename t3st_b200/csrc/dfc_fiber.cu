@@ -58,14 +58,19 @@ __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__
       // index arithmetic.  k0 + 32 j is a multiple of 8, so lane's payload
       // bit is bit (lane & 7) of byte (k0 + 32 j + lane) / 8.
       uint32_t* base = b.words[r] + (b.first_bit + k0 - b.range_base[r]) + lane;
-      uint32_t word[kGroups];
+      uint32_t word[kGroups], in[kGroups];
 #pragma unroll
       for (int j = 0; j < kGroups; ++j) word[j] = base[32 * j];
+      // every load before the first store: a byte load after a word store
+      // could alias it as far as the compiler knows, and would wait for it
+      if (WRITE) {
+#pragma unroll
+        for (int j = 0; j < kGroups; ++j) in[j] = bytes[(k0 + 32 * j + lane) >> 3];
+      }
 #pragma unroll
       for (int j = 0; j < kGroups; ++j) {
         if (WRITE) {
-          const uint32_t in = (static_cast<uint32_t>(bytes[(k0 + 32 * j + lane) >> 3]) >> (lane & 7)) & 1u;
-          base[32 * j] = (word[j] & 0x7FFFFFFFu) | (in << 31);
+          base[32 * j] = (word[j] & 0x7FFFFFFFu) | (((in[j] >> (lane & 7)) & 1u) << 31);
         } else {
           const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
           if (lane < 4) bytes[(k0 + 32 * j) / 8 + lane] = static_cast<uint8_t>(mask >> (8 * lane));
@@ -87,16 +92,17 @@ __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__
         ptr[j] = b.words[r] + (g - b.range_base[r]);
       }
     }
+    uint32_t in[kGroups];
 #pragma unroll
-    for (int j = 0; j < kGroups; ++j) word[j] = ptr[j] ? *ptr[j] : 0u;
+    for (int j = 0; j < kGroups; ++j) {
+      word[j] = ptr[j] ? *ptr[j] : 0u;
+      in[j] = (WRITE && ptr[j]) ? bytes[(k0 + 32 * j + lane) >> 3] : 0u;
+    }
 #pragma unroll
     for (int j = 0; j < kGroups; ++j) {
       const int64_t k = k0 + 32 * j + lane;
       if (WRITE) {
-        if (ptr[j]) {
-          const uint32_t in = (static_cast<uint32_t>(bytes[k >> 3]) >> (k & 7)) & 1u;
-          *ptr[j] = (word[j] & 0x7FFFFFFFu) | (in << 31);
-        }
+        if (ptr[j]) *ptr[j] = (word[j] & 0x7FFFFFFFu) | (((in[j] >> (k & 7)) & 1u) << 31);
       } else {
         const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
         const int64_t byte = (k0 + 32 * j) / 8 + lane;  // lanes 0..3: the group's 4 bytes
