@@ -1,4 +1,4 @@
-"""ZeRO-1 host logic on CPU gloo ranks (world 2 and 4): flat layout, shard
+"""ZeRO-1 host logic on CPU gloo ranks (world 2, 4 and 8): flat layout, shard
 segments, compression + reduce-scatter + step + all-gather wiring, hyper
 sets, consolidated checkpoints, the per-rank sign fiber, and failure
 behaviour.  The CUDA kernels are replaced by an oracle-backed backend (test
@@ -153,7 +153,7 @@ def _worker(rank, world, port, fmt, result_q):
         result_q.put((rank, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world,fmt", [(2, "packed"), (2, "fp32"), (4, "packed")])
+@pytest.mark.parametrize("world,fmt", [(2, "packed"), (2, "fp32"), (4, "packed"), (8, "packed")])
 def test_zero1_matches_simulation(world, fmt):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
