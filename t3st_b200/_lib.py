@@ -18,6 +18,7 @@ from . import build as _build
 LIB_PATH = _build.LIB_PATH
 
 # ---- status codes / enums (mirror include/dfc_b200.h) ----
+ABI_VERSION = 2
 DFC_OK = 0
 DFC_ERR_NULL = -1
 DFC_ERR_ALIGN = -2
@@ -106,7 +107,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_fiber_read": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_fiber_write": ([P, I32, I64, I64, P, P], ctypes.c_int),
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
-        "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, I32, P],
+        "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, I32, P],
                                 ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
         "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
@@ -131,10 +132,33 @@ def lib() -> ctypes.CDLL:
         except OSError as e:  # pragma: no cover - depends on the machine
             raise ImportError(f"cannot load {path}: {e}") from e
         _declare(h)
-        if h.dfc_abi_version() != 1:
+        if h.dfc_abi_version() != ABI_VERSION:
             raise ImportError(f"{path}: unexpected ABI version {h.dfc_abi_version()}")
         _lib = h
     return _lib
+
+
+_host = None
+
+
+def host():
+    """The native host plan module (t3st_b200._dfc_host), built first if it
+    is absent (needs g++ and PyTorch's headers)."""
+    global _host
+    if _host is None:
+        import importlib
+
+        import torch  # noqa: F401  (the extension links against libtorch_python)
+
+        if not os.path.exists(_build.HOST_PATH):
+            _build.build_host()
+        _host = importlib.import_module("t3st_b200._dfc_host")
+    return _host
+
+
+def mt_step_address() -> int:
+    """Address of dfc_mt_step in the loaded library (for the host plan)."""
+    return ctypes.cast(lib().dfc_mt_step, ctypes.c_void_p).value
 
 
 def strerror(status: int) -> str:

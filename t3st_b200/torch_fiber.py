@@ -26,8 +26,15 @@ from typing import Iterable
 
 import numpy as np
 import torch
+from torch.optim.optimizer import _global_optimizer_post_hooks, _global_optimizer_pre_hooks
 
 from . import _lib
+
+_profiler_enabled = torch._C._autograd._profiler_enabled
+
+# optimizer attributes a native step plan depends on: if any of them is
+# rebound, the plan no longer holds
+_PLAN_WATCH = ("param_groups", "state", "enable_fiber", "moment_format", "max_grad_norm")
 
 SIGN_MASK_I32 = -2147483648
 MAGNITUDE_MASK_I32 = 2147483647
@@ -108,6 +115,7 @@ class DFCAdamW(torch.optim.Optimizer):
         self._plan_key = None
         self._plan = None
         self._fast = None
+        self._native = None
         self.initialize_state()
 
     # ---- state (remote/torch_fiber.py:41-66) ----
@@ -142,6 +150,7 @@ class DFCAdamW(torch.optim.Optimizer):
         super().add_param_group(param_group)
         self._plan_key = None
         self._fast = None
+        self._native = None
         if hasattr(self, "enable_fiber"):
             self.initialize_state()
 
@@ -161,6 +170,7 @@ class DFCAdamW(torch.optim.Optimizer):
         super().load_state_dict(state_dict)
         self._plan_key = None
         self._fast = None
+        self._native = None
         if saved_format != self.moment_format:
             convert = (_lib.lib().dfc_pack_moments if self.moment_format == "packed"
                        else _lib.lib().dfc_unpack_moments)
@@ -179,8 +189,32 @@ class DFCAdamW(torch.optim.Optimizer):
                                 torch.cuda.current_stream(t.device).cuda_stream))
 
     # ---- the step (remote/torch_fiber.py:68-117) ----
-    @torch.no_grad()
     def step(self, closure=None):
+        """One DFC-AdamW step over every parameter with a gradient.
+
+        Steady state (no closure, no step hooks, no profiler): the native
+        plan re-checks pointers, dtypes and step counters and launches the
+        fused step (one C call).  Otherwise the step runs inside
+        torch.optim.Optimizer's wrapper (profiler range, pre/post hooks)."""
+        plan = self._native
+        if (plan is not None and closure is None and not self._optimizer_step_pre_hooks
+                and not self._optimizer_step_post_hooks and not _global_optimizer_pre_hooks
+                and not _global_optimizer_post_hooks and not _profiler_enabled()):
+            rc = plan.step()
+            if rc == 1:
+                return None
+            self._native = None
+            if rc < 0:
+                _lib.check("dfc_mt_step", rc)
+        return self._hooked_step(closure)
+
+    # torch.optim.Optimizer wraps a subclass's step() in its profiler/hook
+    # wrapper unless the function says it is already hooked; this step()
+    # applies the same wrapper itself whenever hooks or a profiler are there
+    step.hooked = True
+
+    @torch.no_grad()
+    def _step_impl(self, closure=None):
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -191,6 +225,8 @@ class DFCAdamW(torch.optim.Optimizer):
         self._fast = None
         self._step_general()
         return loss
+
+    _hooked_step = torch.optim.Optimizer.profile_hook_step(_step_impl)
 
     def _step_general(self) -> None:
         work = []  # (param, state, grad, group index)
@@ -245,7 +281,10 @@ class DFCAdamW(torch.optim.Optimizer):
         del keepalive
         n_params = sum(len(g["params"]) for g in self.param_groups)
         if len(work) == n_params and len(devices) == 1 and self._plan_key is not None:
-            self._fast = _FastPlan(self, work, segs, devices[0][0])
+            if self.max_grad_norm is None:
+                self._native = _native_plan(self, work, segs, devices[0][0])
+            if self._native is None:
+                self._fast = _FastPlan(self, work, segs, devices[0][0])
 
     def _build_plan(self, work):
         """Validate every (param, grad, state) triple and lay out the segment
@@ -325,8 +364,27 @@ _DATA_PTR = torch.Tensor.data_ptr
 _STRIDE = torch.Tensor.stride
 
 
+def _native_plan(opt: "DFCAdamW", work, segs, device, launch=None):
+    """The native steady-state plan (t3st_b200._dfc_host.StepPlan) for the
+    descriptors of the step just taken, or None where it does not apply
+    (parameters that are tensor subclasses).  ``launch`` is the address of a
+    function with dfc_mt_step's signature (default: dfc_mt_step itself)."""
+    host = _lib.host()
+    segs = segs.copy()
+    segs["hyper"] = [w[3] for w in work]
+    hyp = np.zeros(len(opt.param_groups), dtype=_lib.HYPER_DTYPE)
+    try:
+        return host.StepPlan([w[0] for w in work], [w[1] for w in work], opt.param_groups, segs,
+                             hyp, opt.mode, device.index or 0,
+                             launch if launch is not None else _lib.mt_step_address(),
+                             opt.__dict__, _PLAN_WATCH)
+    except (TypeError, ValueError):
+        return None
+
+
 class _FastPlan:
-    """Steady-state step: every parameter has a gradient, one device, one
+    """Steady-state step with gradient clipping (max_grad_norm), or over
+    parameters the native plan does not take: every parameter has a gradient, one device, one
     step count shared by all parameters, the same parameter and gradient
     storage as the step that built the plan.  Checking that costs a few
     C-level passes over the parameter list (pointers, dtypes, counters); any
