@@ -16,7 +16,10 @@
  *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
  *    is asynchronous and stream-ordered; none synchronises the host.
  *  - Return value: DFC_OK (0) or a negative DFC_ERR_* code.  Nothing aborts,
- *    nothing allocates device memory, nothing is cached between calls.
+ *    nothing allocates device memory, nothing is cached between calls --
+ *    with one exception, dfc_grad_stats_noalloc: its scratch is a static
+ *    device array of the library, and the array's address on each device is
+ *    looked up once and kept (see its comment).
  *  - Every launch is sized from its arguments; a bad argument is reported
  *    before any launch (nothing is half-applied).
  */
@@ -30,7 +33,7 @@
 extern "C" {
 #endif
 
-#define DFC_ABI_VERSION 1
+#define DFC_ABI_VERSION 2
 
 /* Entry points are the library's only exported symbols (it is built with
  * -fvisibility=hidden). */
@@ -294,13 +297,18 @@ DFC_API int dfc_replay_decode(const uint8_t* records, int64_t record_stride, int
  * ctas_per_sm <= 0: one CTA per 2048-element tile; > 0: a persistent grid of
  * at most that many CTAs per SM, so that the next bucket's dfc_compress_ef
  * (with its own cap) runs beside it instead of after it.
+ * error_flag: NULL, or the device int that dfc_peer_barrier sets when it
+ * gives up.  When it is non-zero as the kernel starts, the kernel returns
+ * without a single load or store: after a barrier time-out no rank reads a
+ * peer's half-written gradients or writes into a stalled peer's parameters,
+ * and this rank's parameters and moments stay as they were.
  */
 DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
                                 const void* comp_multicast, void* param_multicast,
                                 int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                 int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                 int32_t mode, const float* device_grad_scale,
-                                int32_t ctas_per_sm, void* stream);
+                                const int32_t* error_flag, int32_t ctas_per_sm, void* stream);
 
 /*
  * The NVSwitch sum over every rank of numel bf16 values at a multicast
@@ -318,8 +326,11 @@ DFC_API int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64
  * r of every array (release, system scope), then waits until every word of
  * its own array has reached `epoch` (acquire, system scope), for at most
  * timeout_ns; on time-out it stores 1 + the index of the missing rank into
- * *error_flag (device int) and returns.  Epochs must increase by one per
- * call.  One rank per GPU: ranks sharing a GPU may never run concurrently.
+ * *error_flag (device int) and returns.  A flag that is already non-zero
+ * (an earlier barrier gave up) makes the call return at once, storing
+ * nothing into the peers' arrays and waiting for nothing, so a failed step
+ * ends in bounded time on every rank.  Epochs must increase by one per call.
+ * One rank per GPU: ranks sharing a GPU may never run concurrently.
  */
 DFC_API int dfc_peer_barrier(uint32_t* const* slot_ptrs, int32_t n_peers, int32_t rank,
                              uint32_t epoch, int32_t* error_flag, int64_t timeout_ns,

@@ -54,6 +54,7 @@ struct ZeroBatch {
   const uint16_t* comp_mc;          // multicast address of the gradients (nvls kernel)
   float* param_mc;                  // multicast address of the parameters (nvls kernel)
   const float* dev_scale;
+  const int32_t* error;             // a barrier's give-up flag, or null
   int32_t n_peers;
   int32_t rank;
   int32_t n_segs;
@@ -209,6 +210,9 @@ __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const Pe
 template <int MODE, int NP, bool NVLS, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, 4)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
+  // A barrier before this kernel gave up: a peer may be stalled or gone, so
+  // neither its gradients nor its parameter copy may be touched.
+  if (b.error && *static_cast<const volatile int32_t*>(b.error) != 0) return;
   const int32_t tiles = b.tile_base[b.n_segs];
   for (int32_t t = static_cast<int32_t>(blockIdx.x); t < tiles; t += static_cast<int32_t>(gridDim.x)) {
     int lo = 0, hi = b.n_segs;
@@ -309,6 +313,8 @@ struct BarrierArgs {
 __global__ void peer_barrier_kernel(const __grid_constant__ BarrierArgs a) {
   const int q = threadIdx.x;
   if (q >= a.n_peers) return;
+  // an earlier barrier gave up: signal nobody, wait for nobody
+  if (*static_cast<volatile int32_t*>(a.error) != 0) return;
   __threadfence_system();  // this rank's earlier writes, local and remote, come first
   st_release_sys(a.slots[q] + a.rank, a.epoch);
   const uint32_t* mine = a.slots[a.rank] + q;
@@ -336,7 +342,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
                                    int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                    int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                    int32_t mode, const float* device_grad_scale,
-                                   int32_t ctas_per_sm, void* stream) {
+                                   const int32_t* error_flag, int32_t ctas_per_sm, void* stream) {
   using namespace dfc;
   if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers) return DFC_ERR_SIZE;
   if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
@@ -349,6 +355,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     if (!aligned(comp_ptrs[q], 16) || !aligned(param_ptrs[q], 16)) return DFC_ERR_ALIGN;
   if ((comp_multicast == nullptr) != (param_multicast == nullptr)) return DFC_ERR_NULL;
   if (!aligned(comp_multicast, 16) || !aligned(param_multicast, 16)) return DFC_ERR_ALIGN;
+  if (!aligned(error_flag, 4)) return DFC_ERR_ALIGN;
   for (int32_t i = 0; i < n_segments; ++i) {
     const DfcPeerSegment& s = segments[i];
     if (s.numel < 0 || s.offset < 0) return DFC_ERR_SIZE;
@@ -366,6 +373,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
   b.comp_mc = static_cast<const uint16_t*>(comp_multicast);
   b.param_mc = static_cast<float*>(param_multicast);
   b.dev_scale = device_grad_scale;
+  b.error = error_flag;
   b.n_peers = n_peers;
   b.rank = rank;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -293,6 +293,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self._comp_peers, self._h_comp, self._comp_mc = peers(self.comp)
         self._slot_peers, self._h_slots, _ = peers(self.slots)
         self.peer_error = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # the flag as of the end of the last step, copied to the host on the
+        # side stream; read by the next step() without waiting
+        self._peer_error_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._peer_error_copied = None
         self._epoch = 0
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
@@ -312,13 +316,30 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             _lib.ptr(self._slot_arr), self.world, self.rank, self._epoch & 0xFFFFFFFF,
             self.peer_error.data_ptr(), self.barrier_timeout_ns, stream))
 
+    def _check_peer_error(self):
+        """Raise if a barrier of an earlier step gave up.  The flag's copy
+        of the last step is read only if it has already landed (no wait); a
+        later step() or peer_status() sees a copy still in flight."""
+        ev = self._peer_error_copied
+        if ev is not None and ev.query():
+            self._peer_error_copied = None
+            code = int(self._peer_error_host[0])
+            if code:
+                raise RuntimeError(
+                    f"ShardedDFCAdamW: a cross-GPU barrier gave up waiting for rank {code - 1} "
+                    f"after {self.barrier_timeout_ns / 1e9:g} s; the steps since then did not "
+                    f"update parameters or moments (restore a checkpoint)")
+
     def _step_peer(self, rows, index):
         """Bucket b: compress on the caller's stream; then, on a side stream
         that waits for it, a barrier (every rank's bucket-b gradients are
         complete) and the fused step of bucket b -- which runs while the
         caller's stream compresses bucket b+1.  A last barrier (every rank's
         parameters are complete) ends the step; the caller's stream waits
-        for it."""
+        for it.  A barrier that gives up sets peer_error; from then on every
+        fused kernel and barrier of this rank returns at once, touching no
+        memory, and the next step() raises."""
+        self._check_peer_error()
         main = torch.cuda.current_stream(self.device)
         side = self._side
         hyp = kernels.hypers(rows)
@@ -336,9 +357,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     _lib.check("dfc_zero_fused_step", lib.dfc_zero_fused_step(
                         _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self._comp_mc,
                         self._param_mc, self.world, self.rank, _lib.ptr(segs), len(segs),
-                        _lib.ptr(hyp), len(rows), self.mode, None, self.fused_ctas,
-                        side.cuda_stream))
+                        _lib.ptr(hyp), len(rows), self.mode, None, self.peer_error.data_ptr(),
+                        self.fused_ctas, side.cuda_stream))
             self._barrier(side.cuda_stream)
+            with torch.cuda.stream(side):
+                self._peer_error_host.copy_(self.peer_error, non_blocking=True)
+                self._peer_error_copied = side.record_event()
         main.wait_stream(side)
 
     def peer_status(self) -> int:

@@ -1,6 +1,9 @@
 """The C-ABI library loads, exports what the header declares and rejects bad
 arguments before touching the GPU.  CPU only: every call here fails
-validation, so no CUDA call is made."""
+validation, so no CUDA call is made.  The validation tests pass made-up
+device addresses; they are skipped wherever a GPU is visible, so that a
+regression in the validation order could never send such an address to a
+kernel on a real device."""
 
 import ctypes
 import os
@@ -10,6 +13,11 @@ import numpy as np
 import pytest
 
 from t3st_b200 import _lib
+
+# made-up device addresses below: never where a kernel could run
+no_device = pytest.mark.skipif(
+    __import__("torch").cuda.is_available(),
+    reason="passes made-up device addresses; runs only where no GPU is visible")
 
 HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
                       "dfc_b200.h")
@@ -33,7 +41,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_strerror():
     lib = _lib.lib()
-    assert lib.dfc_abi_version() == 1
+    assert lib.dfc_abi_version() == _lib.ABI_VERSION
     for code in range(-9, 1):
         assert _lib.strerror(code) not in ("", "unknown status")
     assert _lib.strerror(-100) == "unknown status"
@@ -55,6 +63,7 @@ def _seg(**kw):
     return s
 
 
+@no_device
 def test_step_rejects_bad_arguments_before_launch():
     lib = _lib.lib()
     h = np.zeros(1, dtype=_lib.HYPER_DTYPE)
@@ -84,6 +93,7 @@ def test_step_rejects_bad_arguments_before_launch():
     assert lib.dfc_mt_step(P(two), 2, P(h), 1, 1, None, None) == _lib.DFC_ERR_SIZE
 
 
+@no_device
 def test_other_entry_points_reject_bad_arguments():
     lib = _lib.lib()
     assert lib.dfc_compress_ef(None, None, None, -1, 0, None) == _lib.DFC_ERR_SIZE
@@ -115,6 +125,22 @@ def test_other_entry_points_reject_bad_arguments():
     assert lib.dfc_fiber_write(_lib.ptr(ranges), 2, 0, 16, None, None) == _lib.DFC_ERR_NULL
     ranges[1]["words"] = 0x2002
     assert lib.dfc_fiber_write(_lib.ptr(ranges), 2, 0, 16, 0x9000, None) == _lib.DFC_ERR_ALIGN
+
+    comps = (ctypes.c_uint64 * 2)(0x10000, 0x20000)
+    params = (ctypes.c_uint64 * 2)(0x30000, 0x40000)
+    segs = np.zeros(1, dtype=_lib.PEERSEG_DTYPE)
+    segs[0] = (0, 64, 0x50000, 0x60000, 0, 0)
+    h = np.zeros(1, dtype=_lib.HYPER_DTYPE)
+
+    def fused(error_flag, n_peers=2, rank=0):
+        return lib.dfc_zero_fused_step(comps, params, None, None, n_peers, rank, _lib.ptr(segs), 1,
+                                       _lib.ptr(h), 1, _lib.MODE_PACKED, None, error_flag, 0, None)
+
+    assert fused(0x70002) == _lib.DFC_ERR_ALIGN  # the barrier's error flag is an int
+    assert fused(0x70000, n_peers=9) == _lib.DFC_ERR_SIZE
+    assert fused(0x70000, rank=2) == _lib.DFC_ERR_SIZE
+    segs[0]["hyper"] = 1
+    assert fused(0x70000) == _lib.DFC_ERR_HYPER
 
 
 def test_library_is_self_contained():
