@@ -15,7 +15,9 @@
 // stand-in symbol, not a device address.  The first call on each device
 // (with that device current) looks the address up once with
 // cudaGetSymbolAddress and caches it; that first call should therefore come
-// before any stream capture.  Every call shares the one array per device and
+// before any stream capture.  The cached address belongs to the device's
+// primary context: after cudaDeviceReset on a device this entry point must
+// not be called again on it in the same process.  Every call shares the one array per device and
 // it keeps the last call's contents; nothing needs clearing, because each
 // call writes every partial record before its second pass reads it.  Calls
 // whose kernels overlap on the GPU (different streams, no ordering) race on

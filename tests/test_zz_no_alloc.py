@@ -63,13 +63,26 @@ def test_noalloc_stats_match_the_scratch_entry_point_on_two_calls(cuda):
 
 
 def test_noalloc_rejects_requests_beyond_the_static_capacity(cuda):
-    g = torch.zeros(16, device=cuda)
-    refs = kernels.grad_refs([g])
-    # claim more elements than the partial-record array can cover; the call
-    # must refuse before launching anything (the pointer is never read)
-    refs["numel"][0] = (_lib.GRAD_STATS_STATIC_RECORDS + 1) * 8192
-    out = torch.empty(_lib.GRADSTATS_DTYPE.itemsize, dtype=torch.uint8, device=cuda)
+    # one more gradient than the partial-record array has records (each
+    # gradient takes at least one): 65,537 one-element slices of one real
+    # buffer, so every descriptor points at memory the call may read.  The
+    # call must refuse before launching anything.
+    n = _lib.GRAD_STATS_STATIC_RECORDS + 1
+    g = torch.zeros(n, device=cuda)
+    refs = np.zeros(n, dtype=_lib.GRADREF_DTYPE)
+    refs["grad"] = g.data_ptr() + 4 * np.arange(n, dtype=np.uint64)
+    refs["numel"] = 1
+    out = torch.full((n * _lib.GRADSTATS_DTYPE.itemsize,), 0xAB, dtype=torch.uint8, device=cuda)
     with torch.cuda.device(cuda):
-        rc = _lib.lib().dfc_grad_stats_noalloc(_lib.ptr(refs), 1, out.data_ptr(),
+        rc = _lib.lib().dfc_grad_stats_noalloc(_lib.ptr(refs), n, out.data_ptr(),
                                                torch.cuda.current_stream(cuda).cuda_stream)
     assert rc == _lib.DFC_ERR_SCRATCH
+    torch.cuda.synchronize()
+    assert int((out != 0xAB).sum()) == 0  # nothing was written
+    # at the capacity itself the same buffers are accepted
+    with torch.cuda.device(cuda):
+        rc = _lib.lib().dfc_grad_stats_noalloc(_lib.ptr(refs), n - 1, out.data_ptr(),
+                                               torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == _lib.DFC_OK
+    st = kernels.stats_to_numpy(out[:(n - 1) * _lib.GRADSTATS_DTYPE.itemsize])
+    assert not st["sumsq"].any() and not st["amax"].any() and not st["nonfinite"].any()
