@@ -95,16 +95,15 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(name: str):
-    """DRAM bytes per launch from a committed ncu summary, if present."""
-    path = os.path.join(REPO, "profiles", name)
+def profiled_traffic(kernel: str):
+    """DRAM bytes (read + written) per launch of ``kernel`` from one ncu
+    capture, kept in profiles/traffic.json; None if absent."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
+        with open(path) as f:
+            return float(json.load(f)[kernel]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
 
 
 class ClockSampler:
@@ -124,7 +123,9 @@ class ClockSampler:
             self.gpu_id = str(device.index or 0)
         self.proc = None
 
-    def start(self):
+    def start(self, wait_s: float = 5.0):
+        """Start sampling; return once the first sample has arrived (or after
+        wait_s), so that nvidia-smi's start-up lies outside a timed region."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.QUERY}",
@@ -135,6 +136,9 @@ class ClockSampler:
             return self
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.perf_counter()
+        while not self.samples and time.perf_counter() - t0 < wait_s:
+            time.sleep(0.02)
         return self
 
     def _read(self):
@@ -370,10 +374,16 @@ def run_reference(args, rank, world):
 # ----------------------------------------------------------------------------
 # our arm, one GPU
 # ----------------------------------------------------------------------------
+LEAD_IN_STEPS = 3  # untimed steps queued ahead of the timed region
+
+
 def run_single(args, device):
     from t3st_b200 import DFCAdamW
     from t3st_b200.workloads import resnet18_cifar_shapes
 
+    # the clock sampler starts before any GPU work, so that nvidia-smi's
+    # start-up is long over when the timed region begins
+    sampler = None if args.no_clocks else ClockSampler(device).start()
     params, flat_p, flat_g, gen, n_params = resnet18_params(device)
     opt = DFCAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
                    moment_format="packed")
@@ -389,9 +399,13 @@ def run_single(args, device):
     K = args.steps
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    sampler = None if args.no_clocks else ClockSampler(device).start()
     torch.cuda.synchronize()
     t_wall = time.perf_counter()
+    # e0 is queued behind a few untimed steps, so the timed region starts
+    # with the GPU busy and the launch queue ahead of it (not with the host
+    # latency of a first launch onto an idle stream)
+    for _ in range(LEAD_IN_STEPS):
+        opt.step()
     e0.record(stream)
     for _ in range(K):
         opt.step()
@@ -417,7 +431,7 @@ def run_single(args, device):
     peak, peak_kind = measured_hbm_peak()
     algo_bytes = STEP_BYTES_PER_PARAM * n_params
     achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
-    traffic = profiled_traffic("dfc_step_resnet18.md")
+    traffic = profiled_traffic("dfc_step_resnet18")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True,
@@ -430,6 +444,9 @@ def run_single(args, device):
             "algorithmic_bytes_per_param": STEP_BYTES_PER_PARAM,
             "l2": "inputs 313 MB per step > 126 MB L2 (no flush)",
             "parallelism": "single GPU",
+            "timed_region": f"CUDA events on the launching stream; e0 queued behind "
+                            f"{LEAD_IN_STEPS} untimed in-flight steps, then K steps, e1, "
+                            f"synchronize",
         },
         "hbm_gbs": algo_bytes * K / (total_ms / 1e3) / 1e9,
         "hbm_pct_of_8tbs": 100.0 * algo_bytes * K / (total_ms / 1e3) / 1e9 / NOMINAL_HBM_GBS,
@@ -752,12 +769,75 @@ ZERO_PARAMS = 1 << 30
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
 
 
+def time_sharded_alone(device, group, K=10):
+    """The same ZeRO-1 workload with a one-rank process group on this GPU
+    (compression + packed step over the whole vector, no exchange): the
+    one-GPU point of the series, measured in the same run.  Returns ms per
+    step (max over the ranks, which all run it at once)."""
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    P = ZERO_PARAMS
+    gen = torch.Generator(device=device).manual_seed(1234)
+    param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
+    opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
+                          moment_format="packed", compress_grads=True, process_group=group)
+    del param
+    opt.flat_grad[:P].normal_(0.0, 1e-3, generator=gen)
+    for _ in range(3):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    del opt
+    torch.cuda.empty_cache()
+    return ms
+
+
+def nccl_all_gather_gbs(P, world, device, reps=5):
+    """Inbound GB/s per rank of NCCL's all-gather of the FP32 vector (each
+    rank receives 4P(N-1)/N bytes): the fabric rate NCCL gets on this box
+    for the parameter broadcast, max time over ranks."""
+    import torch.distributed as dist
+
+    out = torch.empty(P, dtype=torch.float32, device=device)
+    piece = torch.ones(P // world, dtype=torch.float32, device=device)
+    for _ in range(2):
+        dist.all_gather_into_tensor(out, piece)
+    torch.cuda.synchronize()
+    dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dist.all_gather_into_tensor(out, piece)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world, device)
+    del out, piece
+    torch.cuda.empty_cache()
+    return 4 * P * (world - 1) / world / (ms / 1e3) / 1e9
+
+
 def run_sharded(args, rank, world, device):
     import torch.distributed as dist
 
     from t3st_b200.zero import ShardedDFCAdamW
 
+    sampler = ClockSampler(device).start() if (rank == 0 and not args.no_clocks) else None
     P = ZERO_PARAMS
+    peak, peak_kind = measured_hbm_peak()
+    # the one-GPU point of the same workload, every rank at once, no exchange
+    alone_group, _ = dist.new_subgroups(group_size=1)
+    ms_alone = max_over_ranks(time_sharded_alone(device, alone_group), world, device)
+    frac_alone = 38 * P / (ms_alone / 1e3) / 1e9 / peak   # 12 B compress + 26 B step
+    ag_gbs = nccl_all_gather_gbs(P, world, device)
+
     gen = torch.Generator(device=device).manual_seed(1234)  # same params on every rank
     param = torch.nn.Parameter(torch.empty(P, device=device).normal_(0.0, 0.02, generator=gen))
     opt = ShardedDFCAdamW([param], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD,
@@ -776,9 +856,9 @@ def run_sharded(args, rank, world, device):
     K = args.steps
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(device).start() if (rank == 0 and not args.no_clocks) else None
     dist.barrier()
     torch.cuda.synchronize()
+    opt.step()  # untimed lead-in step: e0 is queued behind it
     e0.record(stream)
     for _ in range(K):
         opt.step()
@@ -787,6 +867,8 @@ def run_sharded(args, rank, world, device):
     dist.barrier()
     ms = max_over_ranks(e0.elapsed_time(e1), world, device)
     clocks = sampler.stop() if sampler is not None else {"skipped": "rank > 0 or --no-clocks"}
+    if opt.peer_status():
+        raise RuntimeError(f"a cross-GPU barrier gave up (status {opt.peer_status()})")
     value = P * K / (ms / 1e3)
     # roofline: the slower of the bytes through this rank's HBM and its NVLink
     # bytes.  HBM counts the peers' traffic into this GPU's memory too.
@@ -804,12 +886,14 @@ def run_sharded(args, rank, world, device):
         # their pieces and their FP32 parameter writes here: 6 B/elem of the rest
         hbm_bytes = 12 * P + 26 * P // world + 6 * P * (world - 1) // world
         nvl_bytes = 6 * P * (world - 1) // world  # bf16 RS + FP32 AG, per direction
-    peak, peak_kind = measured_hbm_peak()
     t_hbm = hbm_bytes / (peak * 1e9)
     t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
     roof_rate = P / max(t_hbm, t_nvl)
+    t_nvl_ag = nvl_bytes / (ag_gbs * 1e9)
+    roof_rate_ag = P / max(t_hbm, t_nvl_ag)
     line = None
     if rank == 0:
+        frac = value / roof_rate
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
@@ -828,13 +912,32 @@ def run_sharded(args, rank, world, device):
                 "bucket_elems": opt.bucket, "buckets": opt.n_buckets,
                 "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
+                "timed_region": "CUDA events on the launching stream; e0 queued behind one "
+                                "untimed in-flight step; max over ranks",
             },
             "roofline": {"bound": "nvlink" if t_nvl > t_hbm else "hbm",
                          "achieved": value, "peak": roof_rate, "unit": UNIT,
-                         "frac": value / roof_rate,
+                         "frac": frac,
                          "hbm_bytes_per_rank": hbm_bytes, "nvlink_bytes_per_rank": nvl_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": f"{peak_kind} hbm_gbs",
-                         "nvlink_gbs": NVLINK_GBS, "traffic": None},
+                         "nvlink_gbs": NVLINK_GBS,
+                         "nvlink_source": "measured peer copy per direction on this pool",
+                         "traffic": None},
+            # the same roofline with the fabric rate NCCL's all-gather of the FP32
+            # vector reaches on this box in this run (a pattern-specific rate)
+            "roofline_fabric_measured": {
+                "nvlink_gbs": ag_gbs, "source": "NCCL all_gather_into_tensor of the 2^30 FP32 "
+                                               "vector, inbound bytes per rank / time, this run",
+                "bound": "nvlink" if t_nvl_ag > t_hbm else "hbm", "peak": roof_rate_ag,
+                "unit": UNIT, "frac": value / roof_rate_ag},
+            # the one-GPU point of this workload (measured in this run) and the
+            # scaling efficiency as the north star defines it: roofline fraction
+            # at N over roofline fraction at 1
+            "one_gpu_same_workload": {
+                "value": P / (ms_alone / 1e3), "unit": UNIT, "ms_per_step": ms_alone,
+                "roofline_frac": frac_alone,
+                "roofline": "38 B/elem (12 compression + 26 step) at the measured HBM peak"},
+            "roofline_frac_ratio_vs_1gpu": frac / frac_alone,
             "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport in ("peer", "nvls")
                                  else 2 * opt.n_buckets),
             "clocks": clocks,

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <checkout of YellowJune/T3st>
 
 It imports ``remote/torch_fiber.py`` from the reference (YellowJune/T3st),
 runs its ``DFCAdamW.step`` (:68-117) on CPU tensors with seeded inputs, and
@@ -339,7 +339,9 @@ def case_replay(vb):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("T3ST_REFERENCE"),
+                    required="T3ST_REFERENCE" not in os.environ,
+                    help="checkout of the reference (YellowJune/T3st); default: $T3ST_REFERENCE")
     ap.add_argument("--only", default=None, help="make one case (by file name)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "remote"))
