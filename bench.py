@@ -67,6 +67,11 @@ def parse_args():
                     help="measure only the replay-record codec (one GPU) and print its JSON")
     ap.add_argument("--replay-batch", type=int, default=65536,
                     help="records per codec launch")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="measure only the compression, gradient-statistics and sign-fiber "
+                         "kernels (one GPU) over --elems elements and print their JSON")
+    ap.add_argument("--elems", type=int, default=None,
+                    help="--kernels-only: elements per buffer (default 2^30)")
     ap.add_argument("--no-sharded-1gpu", action="store_true",
                     help="N=1: skip the one-GPU run of the sharded compressed-gradient step")
     ap.add_argument("--no-host-overhead", action="store_true",
@@ -649,46 +654,70 @@ def run_sharded_1gpu(device, peak, peak_kind, K=30):
     ms = e0.elapsed_time(e1) / K
     hbm_bytes = 12 * P + 26 * P  # compression over P, step over P with bf16 gradients
     gbs = hbm_bytes / (ms / 1e3) / 1e9
-    # the compression kernel alone over the whole vector (one launch, 12 B/elem)
-    from t3st_b200 import kernels
-
-    Kc = 10
-    e0.record(stream)
-    for _ in range(Kc):
-        kernels.compress_ef(opt.flat_grad[:P], opt.comp[:P], opt.resid[:P])
-    e1.record(stream)
-    torch.cuda.synchronize()
-    c_ms = e0.elapsed_time(e1) / Kc
-    c_gbs = 12 * P / (c_ms / 1e3) / 1e9
-    # per-buffer gradient statistics (sum of squares, max, non-finite count)
-    # over the FP32 gradient: 4 B/elem read, two passes (tiles, then records)
-    e0.record(stream)
-    for _ in range(Kc):
-        kernels.grad_stats([opt.flat_grad[:P]])
-    e1.record(stream)
-    torch.cuda.synchronize()
-    s_ms = e0.elapsed_time(e1) / Kc
-    s_gbs = 4 * P / (s_ms / 1e3) / 1e9
-    fiber = run_fiber_kernels(opt.exp_avg_sq, device, peak, Kc)
+    launches = 2 * opt.n_buckets
+    del opt
+    torch.cuda.empty_cache()
     out = {"workload": "ShardedDFCAdamW at one rank over the flat 2^30-element FP32 vector: "
                        "bf16 error-feedback compression + packed step (bf16 gradients)",
            "params": P, "steps": K, "ms_per_step": ms, "value": P / (ms / 1e3), "unit": UNIT,
-           "gpu_launches_per_step": 2 * opt.n_buckets,
+           "gpu_launches_per_step": launches,
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                         "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                        "algorithmic_bytes_per_param": 38},
-           "compress_kernel": {"ms_per_launch": c_ms, "elements": P, "launches": Kc,
-                               "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak,
-                                            "unit": "GB/s", "frac": c_gbs / peak,
-                                            "algorithmic_bytes_per_elem": 12}},
-           "grad_stats_kernels": {"ms_per_call": s_ms, "elements": P, "calls": Kc,
-                                  "roofline": {"bound": "hbm", "achieved": s_gbs, "peak": peak,
-                                               "unit": "GB/s", "frac": s_gbs / peak,
-                                               "algorithmic_bytes_per_elem": 4}},
-           "fiber_kernels": fiber}
-    del opt
+                        "algorithmic_bytes_per_param": 38}}
+    out.update(run_kernels(device, peak, P))
     torch.cuda.empty_cache()
     return out
+
+
+def run_kernels(device, peak, P, K=10):
+    """The kernels beside the step, each over P elements on its own buffers
+    (inputs larger than L2 from 2^26 elements on), K launches between CUDA
+    events: the error-feedback compression (12 B/elem), the gradient
+    statistics (4 B/elem read, two passes) and the sign-fiber payload write
+    and read through the C ABI."""
+    from t3st_b200 import kernels
+
+    gen = torch.Generator(device=device).manual_seed(4321)
+    g = torch.empty(P, device=device).normal_(0.0, 1e-3, generator=gen)
+    comp = torch.zeros(P, dtype=torch.int16, device=device)
+    resid = torch.zeros(P, dtype=torch.int16, device=device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        kernels.compress_ef(g, comp, resid)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(K):
+        kernels.compress_ef(g, comp, resid)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    c_ms = e0.elapsed_time(e1) / K
+    c_gbs = 12 * P / (c_ms / 1e3) / 1e9
+    del comp, resid
+    # per-buffer gradient statistics (sum of squares, max, non-finite count)
+    # over the FP32 gradient: 4 B/elem read, two passes (tiles, then records)
+    kernels.grad_stats([g])
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(K):
+        kernels.grad_stats([g])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    s_ms = e0.elapsed_time(e1) / K
+    s_gbs = 4 * P / (s_ms / 1e3) / 1e9
+    # second-moment words for the fiber: the gradient buffer's bits will do
+    fiber = run_fiber_kernels(g, device, peak, K)
+    del g
+    torch.cuda.empty_cache()
+    return {"compress_kernel": {"ms_per_launch": c_ms, "elements": P, "launches": K,
+                                "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak,
+                                             "unit": "GB/s", "frac": c_gbs / peak,
+                                             "algorithmic_bytes_per_elem": 12}},
+            "grad_stats_kernels": {"ms_per_call": s_ms, "elements": P, "calls": K,
+                                   "roofline": {"bound": "hbm", "achieved": s_gbs, "peak": peak,
+                                                "unit": "GB/s", "frac": s_gbs / peak,
+                                                "algorithmic_bytes_per_elem": 4}},
+            "fiber_kernels": fiber}
 
 
 def cpu_model() -> str:
@@ -989,6 +1018,11 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.kernels_only:
+        if rank == 0:
+            peak, _ = measured_hbm_peak()
+            print(json.dumps(run_kernels(device, peak, args.elems or ZERO_PARAMS)), flush=True)
+        return
     if args.replay_only:
         if rank == 0:
             peak, peak_kind = measured_hbm_peak()

@@ -189,9 +189,10 @@ DFC_API int dfc_unpack_moments(uint32_t* words, int64_t n, int32_t second, void*
  * the previous call and recovered exactly from (comp, resid); comp <- s
  * rounded to the nearest bf16 (ties away from zero); resid <- the signed
  * 16-bit residual field.  comp and resid are read and written in place;
- * both start at zero.  ctas_per_sm (1..8; <= 0 means 8) caps the grid at
- * that many 256-thread CTAs per SM, leaving room for a kernel that runs
- * beside it on another stream (the ZeRO-1 pipeline's fused step).
+ * both start at zero.  ctas_per_sm <= 0: one CTA per 2048-element tile, for
+ * a call that has the GPU to itself; 1..8: a persistent grid of at most that
+ * many 256-thread CTAs per SM, leaving room for a kernel that runs beside it
+ * on another stream (the ZeRO-1 pipeline's fused step).
  */
 DFC_API int dfc_compress_ef(const float* grad, uint16_t* comp, uint16_t* resid, int64_t n,
                             int32_t ctas_per_sm, void* stream);

@@ -1,14 +1,29 @@
 // Sign-fiber payload I/O on the device: bit 31 of every second-moment word,
 // concatenated over a list of word ranges, read into or written from a
-// little-endian packed byte buffer (remote/torch_fiber.py:120-185).  One lane
-// per word, so a warp's word accesses are coalesced: a read gathers the 32
-// lanes' bits with __ballot_sync into 4 payload bytes (bit j of the mask is
-// lane j's bit, which is the little-endian bit order of the payload); a
-// write reads its bit from the payload byte and rewrites its own word, so
-// writes never race.  Each warp takes kGroups groups of 32 words per
-// iteration, with every group's word load issued before the first use.  The
-// range list lives in launch parameters (up to kMaxRanges per launch); a call
-// with more ranges is split into launches at byte boundaries of the payload.
+// little-endian packed byte buffer (remote/torch_fiber.py:120-185).
+//
+// Each warp owns one span of 512 consecutive payload bits (= words); a CTA of
+// 8 warps owns 4096, and the grid has one CTA per 4096 bits, dispatched in
+// address order, so the accesses in flight stay in one compact window of
+// the words (a persistent grid-stride form measured 0.78 of the copy
+// bandwidth on reads; its warps drift apart over the whole buffer).
+//
+// Vector path -- the span lies in one range, its first word is 16-byte
+// aligned and the payload pointer 4-byte aligned: lane l moves words
+// 128 j + 4 l .. + 3 of group j (j = 0..3) as one 16-byte access.  Those
+// four words are payload bits 4 l .. 4 l + 3 of the group's 128, i.e. nibble
+// (l & 7) of the group's 32-bit payload word l >> 3 (little-endian bit
+// order).  A read forms each lane's nibble, ORs the 8 nibbles of a 32-bit
+// payload word together with three butterfly shuffles and stores it from
+// one lane; a write loads the payload word and rewrites bit 31 of its four
+// words.  Writes never race: every word belongs to one lane, and every
+// payload word to one 8-lane group.
+// Per-word path -- a span at a range boundary, at the end of the payload, or
+// misaligned: one lane per word, 32-word groups, a ballot gathers the group's
+// 4 payload bytes on a read; each lane looks its range up.
+// The range list lives in launch parameters (up to kMaxRanges per launch); a
+// call with more ranges is split into launches at byte boundaries of the
+// payload.
 #include <algorithm>
 
 #include "dfc_common.cuh"
@@ -38,78 +53,95 @@ __device__ __forceinline__ int find_range(const FiberBatch& b, int64_t g) {
   return lo;
 }
 
-constexpr int kGroups = 8;  // 32-word groups per warp per iteration
+constexpr int kSpan = 512;               // payload bits (words) per warp
+constexpr int kVecGroups = kSpan / 128;  // 16-byte accesses per lane
+constexpr int kWordGroups = 8;           // 32-word groups per per-word pass
+constexpr int kCtaSpan = kSpan * (kThreads / 32);
+
+// Bits [k0, k0 + 32 * kWordGroups) of the launch, one lane per word; r is a
+// range holding bit first_bit + k0 or an earlier one (ranges ascend).
+template <bool WRITE>
+__device__ __forceinline__ void span_by_word(const FiberBatch& b, uint8_t* bytes, int64_t k0,
+                                             int r, int lane) {
+  const int64_t nbytes = (b.n_bits + 7) / 8;
+  uint32_t* ptr[kWordGroups];
+#pragma unroll
+  for (int j = 0; j < kWordGroups; ++j) {
+    const int64_t k = k0 + 32 * j + lane;
+    ptr[j] = nullptr;
+    if (k < b.n_bits) {
+      const int64_t g = b.first_bit + k;
+      while (g >= b.range_base[r + 1]) ++r;
+      ptr[j] = b.words[r] + (g - b.range_base[r]);
+    }
+  }
+  uint32_t word[kWordGroups], in[kWordGroups];
+  // every load before the first store: a byte load after a word store could
+  // alias it as far as the compiler knows, and would wait for it
+#pragma unroll
+  for (int j = 0; j < kWordGroups; ++j) {
+    word[j] = ptr[j] ? *ptr[j] : 0u;
+    in[j] = (WRITE && ptr[j]) ? bytes[(k0 + 32 * j + lane) >> 3] : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kWordGroups; ++j) {
+    const int64_t k = k0 + 32 * j + lane;
+    if (WRITE) {
+      if (ptr[j]) *ptr[j] = (word[j] & 0x7FFFFFFFu) | (((in[j] >> (k & 7)) & 1u) << 31);
+    } else {
+      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
+      const int64_t byte = (k0 + 32 * j) / 8 + lane;  // lanes 0..3: the group's 4 bytes
+      if (lane < 4 && byte < nbytes) bytes[byte] = static_cast<uint8_t>(mask >> (8 * lane));
+    }
+  }
+}
 
 template <bool WRITE>
 __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__ FiberBatch b,
-                                                         uint8_t* bytes) {
+                                                         uint8_t* bytes, int32_t payload_vec) {
   const int lane = threadIdx.x & 31;
-  const int64_t nbytes = (b.n_bits + 7) / 8;
-  const int64_t span = 32 * kGroups;  // payload bits per warp iteration
-  const int64_t n_iter = (b.n_bits + span - 1) / span;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
-       w < n_iter; w += warps) {
-    const int64_t k0 = span * w;  // first payload bit of this iteration (warp-uniform)
-    int r = find_range(b, b.first_bit + k0);
-    if (k0 + span <= b.n_bits && b.first_bit + k0 + span <= b.range_base[r + 1]) {
-      // The whole iteration lies in range r (the common case): one base
-      // pointer, and word (32 j + lane) of it for group j -- no per-word
-      // index arithmetic.  k0 + 32 j is a multiple of 8, so lane's payload
-      // bit is bit (lane & 7) of byte (k0 + 32 j + lane) / 8.
-      uint32_t* base = b.words[r] + (b.first_bit + k0 - b.range_base[r]) + lane;
-      uint32_t word[kGroups], in[kGroups];
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kCtaSpan + (threadIdx.x >> 5) * kSpan;
+  if (k0 >= b.n_bits) return;  // warp-uniform
+  const int r = find_range(b, b.first_bit + k0);
+  const int64_t off = b.first_bit + k0 - b.range_base[r];
+  uint32_t* base = b.words[r] + off;
+  if (payload_vec && k0 + kSpan <= b.n_bits && b.first_bit + k0 + kSpan <= b.range_base[r + 1] &&
+      (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+    uint4* w4 = reinterpret_cast<uint4*>(base) + lane;
+    uint32_t* pw = reinterpret_cast<uint32_t*>(bytes) + k0 / 32 + (lane >> 3);
+    const int shift = 4 * (lane & 7);
+    uint4 W[kVecGroups];
 #pragma unroll
-      for (int j = 0; j < kGroups; ++j) word[j] = base[32 * j];
-      // every load before the first store: a byte load after a word store
-      // could alias it as far as the compiler knows, and would wait for it
-      if (WRITE) {
+    for (int j = 0; j < kVecGroups; ++j) W[j] = __ldcs(w4 + 32 * j);
+    if (WRITE) {
+      uint32_t P[kVecGroups];
 #pragma unroll
-        for (int j = 0; j < kGroups; ++j) in[j] = bytes[(k0 + 32 * j + lane) >> 3];
+      for (int j = 0; j < kVecGroups; ++j) P[j] = pw[4 * j];
+#pragma unroll
+      for (int j = 0; j < kVecGroups; ++j) {
+        const uint32_t nib = P[j] >> shift;
+        W[j].x = (W[j].x & 0x7FFFFFFFu) | (nib << 31);
+        W[j].y = (W[j].y & 0x7FFFFFFFu) | ((nib >> 1) << 31);
+        W[j].z = (W[j].z & 0x7FFFFFFFu) | ((nib >> 2) << 31);
+        W[j].w = (W[j].w & 0x7FFFFFFFu) | ((nib >> 3) << 31);
+        __stcs(w4 + 32 * j, W[j]);
       }
+    } else {
 #pragma unroll
-      for (int j = 0; j < kGroups; ++j) {
-        if (WRITE) {
-          base[32 * j] = (word[j] & 0x7FFFFFFFu) | (((in[j] >> (lane & 7)) & 1u) << 31);
-        } else {
-          const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
-          if (lane < 4) bytes[(k0 + 32 * j) / 8 + lane] = static_cast<uint8_t>(mask >> (8 * lane));
-        }
-      }
-      continue;
-    }
-    // An iteration at a range boundary or at the end of the payload: each
-    // lane finds its own range.
-    uint32_t* ptr[kGroups];
-    uint32_t word[kGroups];
-#pragma unroll
-    for (int j = 0; j < kGroups; ++j) {
-      const int64_t k = k0 + 32 * j + lane;
-      ptr[j] = nullptr;
-      if (k < b.n_bits) {
-        const int64_t g = b.first_bit + k;
-        while (g >= b.range_base[r + 1]) ++r;  // ranges ascend with g
-        ptr[j] = b.words[r] + (g - b.range_base[r]);
+      for (int j = 0; j < kVecGroups; ++j) {
+        uint32_t v = ((W[j].x >> 31) | ((W[j].y >> 31) << 1) | ((W[j].z >> 31) << 2) |
+                      ((W[j].w >> 31) << 3)) << shift;
+        v |= __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+        v |= __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+        v |= __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+        if ((lane & 7) == 0) pw[4 * j] = v;
       }
     }
-    uint32_t in[kGroups];
-#pragma unroll
-    for (int j = 0; j < kGroups; ++j) {
-      word[j] = ptr[j] ? *ptr[j] : 0u;
-      in[j] = (WRITE && ptr[j]) ? bytes[(k0 + 32 * j + lane) >> 3] : 0u;
-    }
-#pragma unroll
-    for (int j = 0; j < kGroups; ++j) {
-      const int64_t k = k0 + 32 * j + lane;
-      if (WRITE) {
-        if (ptr[j]) *ptr[j] = (word[j] & 0x7FFFFFFFu) | (((in[j] >> (k & 7)) & 1u) << 31);
-      } else {
-        const uint32_t mask = __ballot_sync(0xFFFFFFFFu, (word[j] >> 31) != 0u);
-        const int64_t byte = (k0 + 32 * j) / 8 + lane;  // lanes 0..3: the group's 4 bytes
-        if (lane < 4 && byte < nbytes) bytes[byte] = static_cast<uint8_t>(mask >> (8 * lane));
-      }
-    }
+    return;
   }
+#pragma unroll 1
+  for (int h = 0; h < kSpan / (32 * kWordGroups); ++h)
+    span_by_word<WRITE>(b, bytes, k0 + 32 * kWordGroups * h, r, lane);
 }
 
 template <bool WRITE>
@@ -162,11 +194,11 @@ int fiber_call(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit, 
       if (whole == 0) return DFC_ERR_SIZE;  // more than kMaxRanges ranges inside one byte
     }
     b.n_bits = end - first;
-    const int64_t iters = (b.n_bits + 32 * kGroups - 1) / (32 * kGroups);  // warp iterations
-    const int64_t want = (iters + kThreads / 32 - 1) / (kThreads / 32);
-    const int grid = static_cast<int>(
-        std::max<int64_t>(1, std::min<int64_t>(want, resident_ctas(fiber_kernel<WRITE>, kThreads))));
-    fiber_kernel<WRITE><<<grid, kThreads, 0, st>>>(b, bytes + done / 8);
+    const int64_t ctas = (b.n_bits + kCtaSpan - 1) / kCtaSpan;
+    if (ctas > INT32_MAX) return DFC_ERR_SIZE;
+    uint8_t* launch_bytes = bytes + done / 8;
+    fiber_kernel<WRITE><<<static_cast<unsigned>(ctas), kThreads, 0, st>>>(
+        b, launch_bytes, aligned(launch_bytes, 4) ? 1 : 0);
     const int rc = launch_status();
     if (rc != DFC_OK) return rc;
     done += b.n_bits;

@@ -155,6 +155,43 @@ def test_fiber_large_ranges_round_trip(cuda):
     np.testing.assert_array_equal(ch.read_bits(start, count), bits[start:start + count])
 
 
+@pytest.mark.parametrize("word_off", [0, 1, 4])   # first word 16-byte aligned, not, aligned
+@pytest.mark.parametrize("pay_off", [0, 1])       # payload pointer 4-byte aligned, not
+@pytest.mark.parametrize("start", [0, 512, 13])
+def test_fiber_vector_and_word_paths(cuda, word_off, pay_off, start):
+    """One range of ~1M words through the C ABI: 512-bit spans take the
+    16-byte path when the words and the payload pointer allow it, the
+    per-word path otherwise; both give the reference's bit order."""
+    rng = np.random.default_rng(100 * word_off + 10 * pay_off + start)
+    n = (1 << 20) + 37
+    base = torch.from_numpy(rng.integers(0, 2 ** 32, n, dtype=np.uint64).astype(np.uint32)
+                            .view(np.int32)).to(cuda)
+    w = base[word_off:]
+    before = w.cpu().numpy().view(np.uint32).copy()
+    ranges = np.zeros(1, dtype=_lib.WORDRANGE_DTYPE)
+    ranges[0] = (w.data_ptr(), w.numel())
+    count = w.numel() - start - 7
+    nbytes = (count + 7) // 8
+    buf = torch.full((nbytes + 8,), 0x5A, dtype=torch.uint8, device=cuda)
+    out = buf[pay_off:pay_off + nbytes]
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    _lib.check("dfc_fiber_read", lib.dfc_fiber_read(_lib.ptr(ranges), 1, start, count,
+                                                    out.data_ptr(), stream))
+    want = np.packbits((before[start:start + count] >> 31).astype(np.uint8), bitorder="little")
+    np.testing.assert_array_equal(out.cpu().numpy(), want)
+    assert int((buf[pay_off + nbytes:] != 0x5A).sum()) == 0 and (pay_off == 0 or int(buf[0]) == 0x5A)
+    payload = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    out.copy_(torch.from_numpy(payload))
+    _lib.check("dfc_fiber_write", lib.dfc_fiber_write(_lib.ptr(ranges), 1, start, count,
+                                                      out.data_ptr(), stream))
+    after = w.cpu().numpy().view(np.uint32)
+    bits = np.unpackbits(payload, bitorder="little")[:count].astype(np.uint32)
+    expect = before.copy()
+    expect[start:start + count] = (before[start:start + count] & 0x7FFFFFFF) | (bits << 31)
+    np.testing.assert_array_equal(after, expect)
+
+
 def test_clip_coef_and_clipped_step(cuda):
     torch.manual_seed(0)
     shapes = [(300, 77), (1000,), (5,)]
