@@ -148,7 +148,10 @@ typedef struct DfcPeerSegment {
   int32_t reserved;
 } DfcPeerSegment;
 
-/* A run of second-moment words whose bit 31 forms part of the sign fiber. */
+/* A run of second-moment words whose bit 31 forms part of the sign fiber.
+ * words == NULL makes the run a hole of `count` bits that live elsewhere
+ * (in a ZeRO-1 fiber: another rank's pieces): reads return zero bits there,
+ * writes leave it alone. */
 typedef struct DfcWordRange {
   uint32_t* words;
   int64_t count;
@@ -247,7 +250,13 @@ DFC_API int dfc_clip_coef(const DfcGradStats* stats, int32_t n_stats, float max_
  * packed 8 per byte, least-significant bit first
  * (np.packbits(bitorder="little"), remote/torch_fiber.py:178, 184).  A read
  * leaves the unused high bits of the last byte zero; a write consumes
- * exactly n_bits bits.  Only bit 31 of each word is touched.
+ * exactly n_bits bits.  Only bit 31 of each word is touched.  Ranges with
+ * NULL words are holes (zero bits on a read, untouched on a write): with the
+ * other ranks' runs as holes, a ZeRO-1 rank reads or writes its own bits of
+ * the global fiber at their global positions, and a sum of the ranks' read
+ * buffers is the whole fiber.  (The reference's channel,
+ * remote/torch_fiber.py:151-185, addresses one process's tensors; holes
+ * carry the same bit order across every rank's shard.)
  */
 DFC_API int dfc_fiber_read(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit,
                    int64_t n_bits, uint8_t* bytes, void* stream);

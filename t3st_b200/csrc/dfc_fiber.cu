@@ -21,6 +21,9 @@
 // Per-word path -- a span at a range boundary, at the end of the payload, or
 // misaligned: one lane per word, 32-word groups, a ballot gathers the group's
 // 4 payload bytes on a read; each lane looks its range up.
+// Holes -- a range with no words (NULL) stands for bits that live elsewhere
+// (another rank's pieces of a ZeRO-1 fiber): they read as zero and are left
+// alone by a write.
 // The range list lives in launch parameters (up to kMaxRanges per launch); a
 // call with more ranges is split into launches at byte boundaries of the
 // payload.
@@ -72,7 +75,7 @@ __device__ __forceinline__ void span_by_word(const FiberBatch& b, uint8_t* bytes
     if (k < b.n_bits) {
       const int64_t g = b.first_bit + k;
       while (g >= b.range_base[r + 1]) ++r;
-      ptr[j] = b.words[r] + (g - b.range_base[r]);
+      ptr[j] = b.words[r] ? b.words[r] + (g - b.range_base[r]) : nullptr;  // a hole: none
     }
   }
   uint32_t word[kWordGroups], in[kWordGroups];
@@ -104,9 +107,16 @@ __global__ void __launch_bounds__(kThreads) fiber_kernel(const __grid_constant__
   if (k0 >= b.n_bits) return;  // warp-uniform
   const int r = find_range(b, b.first_bit + k0);
   const int64_t off = b.first_bit + k0 - b.range_base[r];
-  uint32_t* base = b.words[r] + off;
-  if (payload_vec && k0 + kSpan <= b.n_bits && b.first_bit + k0 + kSpan <= b.range_base[r + 1] &&
-      (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+  const bool whole = k0 + kSpan <= b.n_bits && b.first_bit + k0 + kSpan <= b.range_base[r + 1];
+  if (whole && b.words[r] == nullptr) {  // the span lies in a hole
+    if (!WRITE) {
+      const int64_t byte0 = k0 / 8;
+      for (int k = lane; k < kSpan / 8; k += 32) bytes[byte0 + k] = 0;
+    }
+    return;
+  }
+  uint32_t* base = b.words[r] ? b.words[r] + off : nullptr;
+  if (payload_vec && whole && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
     uint4* w4 = reinterpret_cast<uint4*>(base) + lane;
     uint32_t* pw = reinterpret_cast<uint32_t*>(bytes) + k0 / 32 + (lane >> 3);
     const int shift = 4 * (lane & 7);
@@ -152,7 +162,7 @@ int fiber_call(const DfcWordRange* ranges, int32_t n_ranges, int64_t start_bit, 
   int64_t total = 0;
   for (int32_t i = 0; i < n_ranges; ++i) {
     if (ranges[i].count < 0) return DFC_ERR_SIZE;
-    if (ranges[i].count > 0 && !ranges[i].words) return DFC_ERR_NULL;
+    // a NULL words pointer is a hole: bits that live elsewhere
     if (!aligned(ranges[i].words, 4)) return DFC_ERR_ALIGN;
     total += ranges[i].count;
   }

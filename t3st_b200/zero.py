@@ -83,6 +83,21 @@ class CudaKernels:
     def convert(self, words, pack: bool, second: bool):
         (kernels.pack_moments if pack else kernels.unpack_moments)(words, second)
 
+    def fiber_read(self, ranges, start_bit: int, n_bits: int, out: torch.Tensor):
+        """Bits [start_bit, start_bit + n_bits) of the word ranges (NULL words:
+        holes, read as zero) packed into the uint8 tensor out."""
+        with torch.cuda.device(out.device):
+            _lib.check("dfc_fiber_read", _lib.lib().dfc_fiber_read(
+                _lib.ptr(ranges), len(ranges), start_bit, n_bits, out.data_ptr(),
+                torch.cuda.current_stream(out.device).cuda_stream))
+
+    def fiber_write(self, ranges, start_bit: int, n_bits: int, src: torch.Tensor):
+        """Write bits of the uint8 tensor src into the ranges (holes skipped)."""
+        with torch.cuda.device(src.device):
+            _lib.check("dfc_fiber_write", _lib.lib().dfc_fiber_write(
+                _lib.ptr(ranges), len(ranges), start_bit, n_bits, src.data_ptr(),
+                torch.cuda.current_stream(src.device).cuda_stream))
+
 
 class ShardedDFCAdamW(torch.optim.Optimizer):
     """ZeRO-1 DFC-AdamW.  Same hyperparameters as DFCAdamW; extra options:
@@ -402,6 +417,48 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     def payload_bit_capacity(self) -> int:
         return sum(v.numel() for v in self.second_moment_tensors()) if self.enable_fiber else 0
 
+    # ---- the global sign fiber across every rank's pieces --------------------
+    # Global bit k is bit 31 of the second moment of element k of the
+    # parameters taken in order (param_groups order, each parameter's elements
+    # in order, alignment padding excluded): the bit the reference's channel
+    # would address on one process holding every parameter
+    # (remote/torch_fiber.py:120-185).  Under ZeRO-1 the bit lives on the rank
+    # whose piece holds that element.
+    def fiber_runs(self) -> list[tuple[int, int, int, int]]:
+        """Every run of the global fiber, in global order: (first global bit,
+        length, owning rank, index of the run's first word in the owner's
+        exp_avg_sq).  A run is one parameter's slice inside one piece; the
+        table is the same on every rank (it follows from the layout)."""
+        runs, g = [], 0
+        for p, off in zip(self.params, self.offsets):
+            n, e = p.numel(), 0
+            while e < n:
+                b, pos = divmod(off + e, self.bucket)
+                q, inside = divmod(pos, self.piece)
+                take = min(n - e, self.piece - inside)
+                runs.append((g + e, take, q, b * self.piece + inside))
+                e += take
+            g += n
+        return runs
+
+    def fiber_owner(self, bit: int) -> tuple[int, int]:
+        """(rank, word index in that rank's exp_avg_sq) of global fiber bit."""
+        import bisect
+
+        runs = self._fiber_runs_cached()
+        starts = [r[0] for r in runs]
+        total = runs[-1][0] + runs[-1][1] if runs else 0
+        if not 0 <= bit < total:
+            raise IndexError("fiber bit out of bounds")
+        g, _, q, w = runs[bisect.bisect_right(starts, bit) - 1]
+        return q, w + (bit - g)
+
+    def _fiber_runs_cached(self):
+        runs = getattr(self, "_fiber_runs", None)
+        if runs is None:
+            runs = self._fiber_runs = self.fiber_runs()
+        return runs
+
     @torch.no_grad()
     def zero_grad(self, set_to_none: bool = False):
         """Zero the flat gradient buffer; the .grad views stay in place."""
@@ -603,3 +660,97 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         for g, saved in zip(self.param_groups, state_dict["param_groups"]):
             g.update({k: v for k, v in saved.items() if k != "params"})
         self._convert_from(state_dict.get("moment_format", "fp32"))
+
+
+class ShardedSignFiberChannel:
+    """The sign fiber of a ShardedDFCAdamW as ONE channel over the whole
+    parameter set, with the interface of TorchSignFiberChannel
+    (remote/torch_fiber.py:120-185): global bit k is the payload bit of
+    element k of the parameters in order (see ShardedDFCAdamW.fiber_runs),
+    whichever rank holds it.
+
+    Every call is collective: every rank of the optimizer's group calls it
+    with the same arguments (and, for writes, the same payload).  A read runs
+    the fiber kernel once per rank over the global window -- the other ranks'
+    runs are holes that read as zero -- and a byte-wise sum over the ranks
+    (each bit comes from exactly one rank, so the sum is their OR) gives every
+    rank the same bytes.  A write runs the kernel once per rank, each storing
+    only its own bits.  For the rank's own bits alone, without a collective,
+    use TorchSignFiberChannel on the optimizer (its local fiber)."""
+
+    def __init__(self, optimizer):
+        if not optimizer.enable_fiber:
+            raise ValueError("optimizer fiber is disabled")
+        import numpy as np
+
+        self.optimizer = optimizer
+        runs = optimizer._fiber_runs_cached()
+        self._ranges = np.zeros(len(runs), dtype=_lib.WORDRANGE_DTYPE)
+        base = optimizer.exp_avg_sq.data_ptr()
+        for i, (_, n, q, w) in enumerate(runs):
+            self._ranges[i] = (base + 4 * w if q == optimizer.rank else 0, n)
+        self._bits = sum(n for _, n, _, _ in runs)
+        self.device = optimizer.exp_avg_sq.device
+
+    @property
+    def bit_capacity(self) -> int:
+        return self._bits
+
+    @property
+    def byte_capacity(self) -> int:
+        return self._bits // 8
+
+    def owner(self, bit: int) -> tuple[int, int]:
+        """(rank, word index in that rank's second-moment shard) of a global bit."""
+        return self.optimizer.fiber_owner(bit)
+
+    def _check(self, start: int, count: int) -> None:
+        if start < 0 or count < 0 or start + count > self._bits:
+            raise IndexError("fiber range out of bounds")
+
+    def _read_dev(self, start: int, count: int) -> torch.Tensor:
+        out = torch.zeros((count + 7) // 8, dtype=torch.uint8, device=self.device)
+        if count:
+            self.optimizer.kernels.fiber_read(self._ranges, start, count, out)
+        if self.optimizer.world > 1:
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.optimizer.group)
+        return out
+
+    def _write_dev(self, start: int, count: int, src: torch.Tensor) -> None:
+        if count:
+            src = src.to(device=self.device, dtype=torch.uint8).contiguous()
+            self.optimizer.kernels.fiber_write(self._ranges, start, count, src)
+
+    @torch.no_grad()
+    def read_bits(self, start: int, count: int):
+        import numpy as np
+
+        self._check(start, count)
+        packed = self._read_dev(int(start), int(count)).cpu().numpy()
+        return np.unpackbits(packed, bitorder="little")[:count] if count else packed
+
+    @torch.no_grad()
+    def write_bits(self, start: int, payload) -> None:
+        import numpy as np
+
+        bits = np.ascontiguousarray(payload, dtype=np.uint8).reshape(-1)
+        if np.any(bits > 1):
+            raise ValueError("payload must be binary")
+        self._check(start, bits.size)
+        self._write_dev(int(start), bits.size,
+                        torch.from_numpy(np.packbits(bits, bitorder="little")))
+
+    def read_bytes(self, start: int, count: int) -> bytes:
+        if start < 0 or count < 0 or start + count > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        return self._read_dev(int(start) * 8, int(count) * 8).cpu().numpy().tobytes()
+
+    def write_bytes(self, start: int, payload) -> None:
+        import numpy as np
+
+        raw = bytes(payload)
+        if start < 0 or start + len(raw) > self.byte_capacity:
+            raise IndexError("fiber byte range out of bounds")
+        self._write_dev(int(start) * 8, len(raw) * 8,
+                        torch.from_numpy(np.frombuffer(raw, dtype=np.uint8).copy()))
+

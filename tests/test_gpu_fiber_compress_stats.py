@@ -192,6 +192,54 @@ def test_fiber_vector_and_word_paths(cuda, word_off, pay_off, start):
     np.testing.assert_array_equal(after, expect)
 
 
+def test_fiber_holes(cuda):
+    """Ranges with NULL words are holes: zero bits on a read, untouched on a
+    write (how a ZeRO-1 rank addresses its own bits of the global fiber).
+    Holes of a few bits and of several whole 512-bit spans, between ranges
+    that take the 16-byte and the per-word paths."""
+    rng = np.random.default_rng(3)
+    layout = [("w", 1000, 0), ("h", 777, 0), ("w", 5000, 3), ("h", 3 * 4096 + 5, 0),
+              ("w", 70000, 0), ("h", 9, 0), ("w", 4096, 1)]
+    ranges = np.zeros(len(layout), dtype=_lib.WORDRANGE_DTYPE)
+    bufs, truth = [], []
+    for i, (kind, n, off) in enumerate(layout):
+        if kind == "w":
+            b = torch.from_numpy(rng.integers(0, 2 ** 32, n + off, dtype=np.uint64)
+                                 .astype(np.uint32).view(np.int32)).to(cuda)
+            bufs.append((b, off, n))
+            ranges[i] = (b.data_ptr() + 4 * off, n)
+            truth.append((b[off:].cpu().numpy().view(np.uint32) >> 31).astype(np.uint8))
+        else:
+            ranges[i] = (0, n)
+            truth.append(np.zeros(n, np.uint8))
+    bits = np.concatenate(truth)
+    total = bits.size
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    for start, count in [(0, total), (1003, total - 2000), (512 * 30, 4096 * 2)]:
+        out = torch.full(((count + 7) // 8,), 0xFF, dtype=torch.uint8, device=cuda)
+        _lib.check("dfc_fiber_read", lib.dfc_fiber_read(_lib.ptr(ranges), len(ranges), start,
+                                                        count, out.data_ptr(), stream))
+        want = np.packbits(bits[start:start + count], bitorder="little")
+        np.testing.assert_array_equal(out.cpu().numpy(), want)
+    before = [b.cpu().numpy().view(np.uint32).copy() for b, _, _ in bufs]
+    payload = rng.integers(0, 256, (total + 7) // 8, dtype=np.uint8)
+    src = torch.from_numpy(payload).to(cuda)
+    _lib.check("dfc_fiber_write", lib.dfc_fiber_write(_lib.ptr(ranges), len(ranges), 0, total,
+                                                      src.data_ptr(), stream))
+    pbits = np.unpackbits(payload, bitorder="little")[:total].astype(np.uint32)
+    pos = 0
+    k = 0
+    for kind, n, off in layout:
+        if kind == "w":
+            b, _, _ = bufs[k]
+            want = before[k].copy()
+            want[off:] = (want[off:] & 0x7FFFFFFF) | (pbits[pos:pos + n] << 31)
+            np.testing.assert_array_equal(b.cpu().numpy().view(np.uint32), want)
+            k += 1
+        pos += n
+
+
 def test_clip_coef_and_clipped_step(cuda):
     torch.manual_seed(0)
     shapes = [(300, 77), (1000,), (5,)]

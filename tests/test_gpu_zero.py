@@ -126,6 +126,38 @@ def _free_port():
     return port
 
 
+def _fiber_check(rank, world, device):
+    """The global sign fiber across the ranks' shards (real kernels, NCCL
+    sum of the ranks' reads): a payload written by every rank lands in the
+    owning ranks' words and reads back whole on every rank."""
+    from t3st_b200.zero import ShardedDFCAdamW, ShardedSignFiberChannel
+
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter((torch.randn(s) * 0.02).to(device)) for s in SHAPES]
+    opt = ShardedDFCAdamW(params, lr=1e-3, moment_format="packed", bucket_elems=8192,
+                          transport="nccl")
+    ch = ShardedSignFiberChannel(opt)
+    total = sum(p.numel() for p in params)
+    assert ch.bit_capacity == total
+    rng = np.random.default_rng(9)
+    bits = rng.integers(0, 2, total).astype(np.uint8)
+    ch.write_bits(0, bits)
+    torch.cuda.synchronize()
+    mine = opt.exp_avg_sq.view(torch.int32).cpu().numpy().view(np.uint32) >> 31
+    for g, n, q, w in opt.fiber_runs():
+        if q == rank:
+            np.testing.assert_array_equal(mine[w:w + n], bits[g:g + n])
+    np.testing.assert_array_equal(ch.read_bits(0, total), bits)
+    payload = rng.bytes(ch.byte_capacity - 11)
+    ch.write_bytes(11, payload)
+    assert ch.read_bytes(11, len(payload)) == payload
+    # the payload survives a step (bit 31 of the second moment is kept)
+    for p in params:
+        p.grad.normal_(0.0, 1e-3)
+    opt.step()
+    assert ch.read_bytes(11, len(payload)) == payload
+
+
 def _worker(rank, world, port, transport, q, kw):
     try:
         import datetime
@@ -139,7 +171,10 @@ def _worker(rank, world, port, transport, q, kw):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
-        _run(rank, world, dev, True, transport, **kw)
+        if transport == "fiber":
+            _fiber_check(rank, world, dev)
+        else:
+            _run(rank, world, dev, True, transport, **kw)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
@@ -178,6 +213,13 @@ def test_sharded_on_two_gpus(transport):
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
     _spawn(2, transport)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_global_fiber_on_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _spawn(world, "fiber")
 
 
 @pytest.mark.parametrize("transport", ["peer", "nvls"])

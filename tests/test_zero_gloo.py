@@ -29,6 +29,30 @@ class OracleBackend:
             gg = g.view(torch.int16).numpy().view(np.uint16) if g.dtype == torch.bfloat16 else g.numpy()
             O.step(mode, h, p.numpy(), gg, m.numpy().view(np.uint32), v.numpy().view(np.uint32))
 
+    # the fiber kernels' contract (include/dfc_b200.h): the concatenated
+    # ranges' bit 31, NULL words = a hole (zero on a read, left alone on a write)
+    @staticmethod
+    def _words(ptr, n):
+        import ctypes
+
+        return np.ctypeslib.as_array((ctypes.c_uint32 * n).from_address(int(ptr)))
+
+    def fiber_read(self, ranges, start, count, out):
+        bits = np.concatenate([(self._words(w, n) >> 31).astype(np.uint8) if w else
+                               np.zeros(n, np.uint8) for w, n in ranges])
+        out.numpy()[:] = np.packbits(bits[start:start + count], bitorder="little")
+
+    def fiber_write(self, ranges, start, count, src):
+        bits = np.unpackbits(src.numpy(), bitorder="little")[:count].astype(np.uint32)
+        pos = 0
+        for w, n in ranges:
+            lo, hi = max(pos, start), min(pos + n, start + count)
+            if w and lo < hi:
+                words = self._words(w, n)
+                sl = slice(lo - pos, hi - pos)
+                words[sl] = (words[sl] & 0x7FFFFFFF) | (bits[lo - start:hi - start] << 31)
+            pos += n
+
     def convert(self, words, pack, second):
         w = words.numpy().view(np.uint32)
         if second:
@@ -192,6 +216,76 @@ def _dying_worker(rank, world, port, result_q):
             result_q.put((rank, "error: " + str(e)[:60]))
     except BaseException:
         result_q.put((rank, traceback.format_exc()))
+
+
+def _fiber_worker(rank, world, port, result_q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from t3st_b200.zero import ShardedDFCAdamW, ShardedSignFiberChannel
+
+        torch.manual_seed(0)
+        params = [torch.nn.Parameter(torch.randn(s) * 0.02) for s in SHAPES]
+        opt = ShardedDFCAdamW(params, lr=1e-3, backend=OracleBackend(), bucket_elems=256)
+        sizes = [p.numel() for p in params]
+        total = sum(sizes)
+        # the run table against a per-element walk of the layout
+        runs = opt.fiber_runs()
+        assert runs[0][0] == 0 and sum(r[1] for r in runs) == total
+        assert all(a[0] + a[1] == b[0] for a, b in zip(runs, runs[1:]))
+        g = 0
+        for p, off in zip(params, opt.offsets):
+            for e in range(0, p.numel(), 7):
+                flat = off + e
+                b, pos = divmod(flat, opt.bucket)
+                want = (pos // opt.piece, b * opt.piece + pos % opt.piece)
+                assert opt.fiber_owner(g + e) == want, (g + e, want)
+            g += p.numel()
+        local = opt.exp_avg_sq.numel()
+        assert all(0 <= w and w + n <= local for _, n, q, w in runs if q == rank)
+        # collective write, then collective reads, through the global channel
+        ch = ShardedSignFiberChannel(opt)
+        assert ch.bit_capacity == total
+        rng = np.random.default_rng(5)  # the same payload on every rank
+        bits = rng.integers(0, 2, total).astype(np.uint8)
+        ch.write_bits(0, bits)
+        mine = opt.exp_avg_sq.view(torch.int32).numpy().view(np.uint32) >> 31
+        for gk, n, q, w in runs:
+            if q == rank:
+                np.testing.assert_array_equal(mine[w:w + n], bits[gk:gk + n])
+        np.testing.assert_array_equal(ch.read_bits(0, total), bits)
+        np.testing.assert_array_equal(ch.read_bits(13, 1001), bits[13:1014])
+        payload = rng.bytes(ch.byte_capacity - 3)
+        ch.write_bytes(3, payload)
+        assert ch.read_bytes(3, len(payload)) == payload
+        with pytest.raises(IndexError):
+            ch.read_bits(total - 2, 3)
+        dist.barrier()
+        dist.destroy_process_group()
+        result_q.put((rank, "ok"))
+    except BaseException:
+        result_q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_global_fiber_across_shards(world):
+    """Global fiber bit -> (rank, word) mapping and the collective channel
+    over every rank's pieces, on gloo ranks with the oracle backend."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fiber_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert res[r] == "ok", res[r]
 
 
 def test_lost_rank_surfaces_as_error_not_hang():
