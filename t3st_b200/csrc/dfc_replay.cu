@@ -12,8 +12,11 @@
 //                final value 0xFFFFFFFF) of bytes [0, 1544), little-endian
 //   [1548, 1552) zero
 //
-// One warp per record at a time (a persistent grid of 8 CTAs per SM, each
-// warp looping over records).  The warp stages the record in shared memory with
+// One warp per record, one CTA per 8 consecutive records, CTAs dispatched in
+// address order (a persistent grid-stride form ran at 0.94 / 0.84 of the copy
+// bandwidth for encode / decode, this one at 0.99 / 0.94).  The CRC tables
+// are compile-time constants in device memory, copied into shared memory as
+// a CTA starts.  The warp stages the record in shared memory with
 // coalesced 16-byte loads or stores, and splits the CRC: lane k runs the
 // table-driven CRC over its own 48-byte run of the record (lane 0 also over
 // the 8-byte header, starting from 0xFFFFFFFF; the others from 0), then
@@ -82,18 +85,28 @@ const Shifts& shifts() {
 // i followed by k zero bytes, t[k][i] = (t[k-1][i] >> 8) ^ t[0][t[k-1][i] & 0xFF].
 // A 32-bit word x = c ^ (4 message bytes) then advances the remainder with
 // four independent lookups: t[3][x0] ^ t[2][x1] ^ t[1][x2] ^ t[0][x3].
-__device__ __forceinline__ void build_tables(uint32_t (*t)[256]) {
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+struct CrcTables {
+  uint32_t t[4][256];
+};
+
+constexpr CrcTables make_crc_tables() {
+  CrcTables r{};
+  for (int i = 0; i < 256; ++i) {
     uint32_t c = static_cast<uint32_t>(i);
     for (int k = 0; k < 8; ++k) c = (c >> 1) ^ ((c & 1u) ? kPoly : 0u);
-    t[0][i] = c;
+    r.t[0][i] = c;
   }
+  for (int k = 1; k < 4; ++k)
+    for (int i = 0; i < 256; ++i) r.t[k][i] = (r.t[k - 1][i] >> 8) ^ r.t[0][r.t[k - 1][i] & 0xFFu];
+  return r;
+}
+
+// Constant data of the library, fixed at compile time (no allocation).
+__device__ const CrcTables g_crc_tables = make_crc_tables();
+
+__device__ __forceinline__ void load_tables(uint32_t (*t)[256]) {
+  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) t[i >> 8][i & 255] = g_crc_tables.t[i >> 8][i & 255];
   __syncthreads();
-  for (int k = 1; k < 4; ++k) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x)
-      t[k][i] = (t[k - 1][i] >> 8) ^ t[0][t[k - 1][i] & 0xFFu];
-    __syncthreads();
-  }
 }
 
 // CRC-32 of the record staged at rec (bytes [0, 1544)), all 32 lanes.
@@ -132,16 +145,16 @@ struct EncodeArgs {
   Shifts sh;
 };
 
-// Persistent: each warp takes records warp, warp + W, ... (W = warps in the grid).
+// Warp w of CTA c encodes record 8 c + w.
 __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant__ EncodeArgs a) {
   __shared__ uint32_t tables[4][256];
   __shared__ __align__(16) uint8_t stage[kWarps][kRecordBytes];
-  build_tables(tables);
+  load_tables(tables);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* rec = stage[warp];
   uint16_t* packed = reinterpret_cast<uint16_t*>(rec + kHeader);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < a.n; r += stride) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (r < a.n) {
     const float4* src = reinterpret_cast<const float4*>(a.images + r * a.image_stride);
 #pragma unroll 4
     for (int i = lane; i < kPixels / 4; i += 32) {
@@ -165,7 +178,6 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
     uint4* dst = reinterpret_cast<uint4*>(a.records + r * a.record_stride);
     const uint4* s4 = reinterpret_cast<const uint4*>(rec);
     for (int i = lane; i < kRecordBytes / 16; i += 32) dst[i] = s4[i];
-    __syncwarp();  // the stage is rewritten by the next record
   }
 }
 
@@ -180,20 +192,31 @@ struct DecodeArgs {
   Shifts sh;
 };
 
+// q / 15 for a 4-bit q, correctly rounded (what the reference's
+// q.astype(float32) / 15 gives): y = q * RN(1/15) is corrected by one
+// residual step, e = fma(-15, y, q), y + e * RN(1/15).  With 16 possible
+// inputs this is checked exhaustively (tests/test_replay_oracle.py) rather
+// than argued; it replaces two shared-memory table lookups per 4 pixels,
+// which held the decode at 0.84 of the copy bandwidth (MIO throttle).
+__device__ __forceinline__ float nibble_over_15(uint32_t q) {
+  const float r = 0.0666666701436042785644531f;  // RN(1/15) = 0x3D888889
+  const float x = static_cast<float>(q);
+  const float y = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-15.0f, y, x);
+  return __fmaf_rn(e, r, y);
+}
+
+// Warp w of CTA c decodes record 8 c + w.
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeArgs a) {
   __shared__ uint32_t tables[4][256];
-  __shared__ float2 pair[256];  // byte -> (low nibble / 15, high nibble / 15)
   __shared__ __align__(16) uint8_t stage[kWarps][kRecordBytes];
-  for (int t = threadIdx.x; t < 256; t += blockDim.x)
-    pair[t] = make_float2(__fdiv_rn(static_cast<float>(t & 15), 15.0f),
-                          __fdiv_rn(static_cast<float>(t >> 4), 15.0f));
-  build_tables(tables);
+  load_tables(tables);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* rec = stage[warp];
   uint4* s4 = reinterpret_cast<uint4*>(rec);
   const uint16_t* packed = reinterpret_cast<const uint16_t*>(rec + kHeader);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp; r < a.n; r += stride) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (r < a.n) {
     const uint4* src = reinterpret_cast<const uint4*>(a.records + r * a.record_stride);
     for (int i = lane; i < kRecordBytes / 16; i += 32) s4[i] = __ldg(src + i);
     __syncwarp();
@@ -202,8 +225,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 #pragma unroll 4
     for (int i = lane; i < kPixels / 4; i += 32) {
       const uint32_t b = packed[i];
-      const float2 lo = pair[b & 0xFFu], hi = pair[b >> 8];
-      dst[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      __stcs(dst + i, make_float4(nibble_over_15(b & 15u), nibble_over_15((b >> 4) & 15u),
+                                  nibble_over_15((b >> 8) & 15u), nibble_over_15(b >> 12)));
     }
     const uint32_t crc = record_crc(rec, tables, a.sh, lane);
     if (lane == 0) {
@@ -214,23 +237,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       a.status[r] = w[0] != 0x42344643u ? DFC_RECORD_BAD_MAGIC
                                         : (stored != crc ? DFC_RECORD_BAD_CRC : DFC_RECORD_OK);
     }
-    __syncwarp();  // the stage is rewritten by the next record
   }
 }
 
-// One CTA per 8 records, at most as many CTAs as are resident at once (one
-// wave): SMs x resident CTAs per SM for this kernel.
-template <typename Kernel>
-int grid_for(Kernel kernel, int64_t n) {
-  int dev = 0, sms = 148, per_sm = 1;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
-  const int64_t need = (n + kWarps - 1) / kWarps;
-  return static_cast<int>(std::min<int64_t>(need, static_cast<int64_t>(sms) * per_sm));
-}
+// One CTA per 8 records.
+int64_t grid_for(int64_t n) { return (n + kWarps - 1) / kWarps; }
 
 }  // namespace
 }  // namespace dfc
@@ -254,7 +265,8 @@ extern "C" int dfc_replay_encode(const float* images, int64_t image_stride, cons
   a.record_stride = record_stride;
   a.n = n_records;
   a.sh = shifts();
-  encode_kernel<<<grid_for(encode_kernel, n_records), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  if (grid_for(n_records) > INT32_MAX) return DFC_ERR_SIZE;
+  encode_kernel<<<static_cast<unsigned>(grid_for(n_records)), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 
@@ -277,6 +289,7 @@ extern "C" int dfc_replay_decode(const uint8_t* records, int64_t record_stride, 
   a.status = status;
   a.n = n_records;
   a.sh = shifts();
-  decode_kernel<<<grid_for(decode_kernel, n_records), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  if (grid_for(n_records) > INT32_MAX) return DFC_ERR_SIZE;
+  decode_kernel<<<static_cast<unsigned>(grid_for(n_records)), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }

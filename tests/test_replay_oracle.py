@@ -105,3 +105,31 @@ def test_mirror_composite_channel_bounds():
     assert c.read_bytes(0, 12) == b"\0\0\0abcdef\0\0\0"
     with pytest.raises(IndexError):
         c.read_bytes(10, 3)
+
+
+def _rn32(x):
+    """A Fraction rounded to the nearest FP32 value, ties to even."""
+    from fractions import Fraction
+
+    f = np.float32(float(x))
+    cands = [np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))]
+    return min(cands, key=lambda c: (abs(Fraction(float(c)) - x),
+                                     int(np.array(c).view(np.uint32)) & 1))
+
+
+def test_decode_nibble_division_is_correctly_rounded():
+    """The decode kernel forms q / 15 as y = q * RN(1/15), e = fma(-15, y, q),
+    fma(e, RN(1/15), y).  For every 4-bit q this equals the correctly
+    rounded q / 15 that the reference's q.astype(float32) / 15 produces
+    (remote/vision_benchmark.py:92-100); checked here in exact arithmetic."""
+    from fractions import Fraction
+
+    F = lambda v: Fraction(float(v))  # noqa: E731
+    r = _rn32(Fraction(1, 15))
+    assert np.array(r).view(np.uint32) == 0x3D888889
+    for q in range(16):
+        y = _rn32(q * F(r))
+        e = _rn32(q - 15 * F(y))          # fma: one rounding of the exact value
+        got = _rn32(F(e) * F(r) + F(y))   # fma
+        want = np.float32(q) / np.float32(15)
+        assert got == want and _rn32(Fraction(q, 15)) == want, q
