@@ -83,6 +83,9 @@ def parse_args():
                     help="N>1 peer/nvls: CTAs per SM of the fused kernel (0: one per tile)")
     ap.add_argument("--bucket-elems", type=int, default=None,
                     help="N>1: elements per pipelined bucket (default: ShardedDFCAdamW's)")
+    ap.add_argument("--side-priority", type=int, default=None,
+                    help="N>1 peer/nvls: CUDA priority of the fused kernel's stream "
+                         "(lower is higher; default: ShardedDFCAdamW's)")
     ap.add_argument("--compress-ctas", type=int, default=None,
                     help="N>1 peer/nvls: CTAs per SM of the compression beside it (0: 8)")
     return ap.parse_args()
@@ -873,6 +876,8 @@ def run_sharded(args, rank, world, device):
                           moment_format="packed", transport=args.transport,
                           fused_ctas_per_sm=args.fused_ctas,
                           compress_ctas_per_sm=args.compress_ctas,
+                          **({} if args.side_priority is None else
+                             {"side_stream_priority": args.side_priority}),
                           **({} if args.bucket_elems is None else
                              {"bucket_elems": args.bucket_elems}))
     del param
@@ -940,6 +945,7 @@ def run_sharded(args, rank, world, device):
                 "fused_ctas_per_sm": opt.fused_ctas,
                 "bucket_elems": opt.bucket, "buckets": opt.n_buckets,
                 "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
+                "side_stream_priority": opt.side_stream_priority,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
                 "timed_region": "CUDA events on the launching stream; e0 queued behind one "
                                 "untimed in-flight step; max over ranks",

@@ -121,7 +121,12 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     8 ranks 9.0 / 8.0 / 11.2.  So peer up to 4 ranks, nvls
                     beyond where the node has NVLink multicast, else peer
     fused_ctas_per_sm, compress_ctas_per_sm
-                    grid caps of the peer/nvls pipeline (defaults measured)
+                    grid caps of the peer/nvls pipeline (defaults measured;
+                    compress_ctas_per_sm=0: the uncapped tile compression)
+    side_stream_priority
+                    CUDA priority of the stream that runs the barriers and the
+                    fused kernel (lower is higher; PyTorch clamps to the
+                    device's range)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -131,7 +136,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  compress_grads: bool | None = None, average_grads: bool = True,
                  bucket_elems: int = DEFAULT_BUCKET, transport: str = "auto",
                  barrier_timeout_s: float = 30.0, backend=None,
-                 fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None):
+                 fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None,
+                 side_stream_priority: int = 0):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -155,6 +161,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         if self.transport in ("peer", "nvls") and not self.compress:
             raise ValueError("the peer and nvls transports reduce bf16 compressed gradients")
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
+        self.side_stream_priority = int(side_stream_priority)
         # Peer and nvls transports: the fused kernel of bucket b and the
         # compression of bucket b+1 run on two streams.  The compression grid
         # is capped so that the fused kernel finds room on every SM beside it;
@@ -323,7 +330,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             segs = [((p.data_ptr() - self.flat_param.data_ptr()) // 4, p.numel(), m.data_ptr(),
                      v.data_ptr(), 0, 0) for p, _, m, v in group_segs]
             self._peer_segs.append(np.array(segs, dtype=_lib.PEERSEG_DTYPE))
-        self._side = torch.cuda.Stream(self.device)
+        self._side = torch.cuda.Stream(self.device, priority=self.side_stream_priority)
 
     def _barrier(self, stream):
         self._epoch += 1
