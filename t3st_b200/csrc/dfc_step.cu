@@ -13,11 +13,13 @@
 // and an IEEE square root are needed for bit-exactness), so latency is hidden
 // by occupancy rather than by unrolling: 256 threads x 1 float4 per stream,
 // 32 registers, 8 CTAs (2048 threads) per SM, i.e. 128 KB of loads in flight
-// per SM while other warps compute.  Unroll 4 at 86 registers (2 CTAs per
-// SM) reached 86% of the copy bandwidth on the 62-tensor ResNet-18 step, this
-// shape 96%.  Launched with programmatic dependent launch, back-to-back steps
-// overlap one grid's last wave with the next grid's start: 100% of the
-// measured copy bandwidth (233.9 G param-updates/s).
+// per SM while other warps compute.  On the 62-tensor ResNet-18 step (11.2 M
+// params, bench.py --steps 20 / 2000): this shape 232.8 / 234.2 G
+// param-updates/s, 1.00 of the measured copy bandwidth; 2 float4 per stream
+// per thread at 4 CTAs per SM 229.9-231.8; unroll 4 at 2 CTAs per SM 86% of
+// the copy bandwidth.  Launched with programmatic dependent launch, so that
+// back-to-back steps overlap one grid's last wave with the next grid's start
+// (49.6 -> 47.8 us per step).
 //
 // The element arithmetic (remote/torch_fiber.py:90-116, explicit rounding)
 // lives in dfc_step_elem.cuh, shared with the fused ZeRO-1 kernel.
