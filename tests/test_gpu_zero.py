@@ -215,6 +215,34 @@ def test_sharded_on_two_gpus(transport):
     _spawn(2, transport)
 
 
+def test_global_fiber_one_rank(cuda):
+    """ShardedSignFiberChannel at one rank (real kernels): global bit k is
+    element k of the parameters in order, padding between parameters
+    excluded, so it agrees with the local channel over the shard's views and
+    survives a step."""
+    from t3st_b200 import TorchSignFiberChannel
+    from t3st_b200.zero import ShardedDFCAdamW, ShardedSignFiberChannel
+
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter((torch.randn(s) * 0.02).to(cuda)) for s in SHAPES]
+    opt = ShardedDFCAdamW(params, lr=1e-3, moment_format="packed", compress_grads=True,
+                          bucket_elems=8192)
+    ch = ShardedSignFiberChannel(opt)
+    local = TorchSignFiberChannel(opt)
+    total = sum(p.numel() for p in params)
+    assert ch.bit_capacity == total == local.bit_capacity
+    rng = np.random.default_rng(2)
+    bits = rng.integers(0, 2, total).astype(np.uint8)
+    ch.write_bits(0, bits)
+    np.testing.assert_array_equal(local.read_bits(0, total), bits)
+    np.testing.assert_array_equal(ch.read_bits(5, total - 9), bits[5:total - 4])
+    assert ch.owner(total - 1)[0] == 0
+    for p in params:
+        p.grad.normal_(0.0, 1e-3)
+    opt.step()
+    np.testing.assert_array_equal(ch.read_bits(0, total), bits)
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_global_fiber_on_gpus(world):
     if torch.cuda.device_count() < world:
