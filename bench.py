@@ -1001,6 +1001,10 @@ def run_sharded(args, rank, world, device):
                 "roofline_frac": frac_alone,
                 "roofline": "38 B/elem (12 compression + 26 step) at the measured HBM peak"},
             "roofline_frac_ratio_vs_1gpu": frac / frac_alone,
+            # the same ratio with the NVLink term at the NCCL bus bandwidth measured in
+            # this run (the all-gather rate above), as the sharded roofline is defined
+            # over the measured NCCL bandwidth; the line above uses 770 GB/s
+            "roofline_frac_ratio_vs_1gpu_nccl_rate": (value / roof_rate_ag) / frac_alone,
             "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport in ("peer", "nvls")
                                  else 2 * opt.n_buckets),
             "clocks": clocks,
