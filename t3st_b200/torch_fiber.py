@@ -146,6 +146,22 @@ class DFCAdamW(torch.optim.Optimizer):
             return _lib.MODE_PACKED
         return _lib.MODE_SIGNFIBER if self.enable_fiber else _lib.MODE_PLAIN
 
+    # torch.optim.Optimizer pickles defaults, state and param_groups only; the
+    # moment format and options travel too, the step plans are rebuilt
+    def __getstate__(self):
+        st = super().__getstate__()
+        st.update(enable_fiber=self.enable_fiber, moment_format=self.moment_format,
+                  max_grad_norm=self.max_grad_norm)
+        return st
+
+    def __setstate__(self, state):
+        state = dict(state)
+        self.enable_fiber = bool(state.pop("enable_fiber", True))
+        self.moment_format = state.pop("moment_format", "fp32")
+        self.max_grad_norm = state.pop("max_grad_norm", None)
+        super().__setstate__(state)
+        self._plan_key = self._plan = self._fast = self._native = None
+
     def add_param_group(self, param_group) -> None:
         super().add_param_group(param_group)
         self._plan_key = None

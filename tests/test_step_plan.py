@@ -68,3 +68,21 @@ def test_plan_refuses_what_it_cannot_follow(monkeypatch):
     params[2].grad = torch.zeros(params[2].shape[::-1]).permute(2, 1, 0)  # other strides
     assert not opt._fast.try_step(opt)
     assert not calls
+
+
+def test_copy_and_pickle_keep_format_and_drop_plans():
+    """An optimizer that is deep-copied or pickled keeps its moment format
+    and options, and rebuilds its step plans on the next step."""
+    import copy
+    import pickle
+
+    params = [torch.nn.Parameter(torch.zeros(3))]
+    opt = DFCAdamW(params, lr=1e-3, enable_fiber=False, moment_format="packed",
+                   max_grad_norm=2.0)
+    opt._native = object()  # stands for a plan bound to the original's storage
+    for twin in (copy.deepcopy(opt), pickle.loads(pickle.dumps(opt))):
+        assert twin.enable_fiber is False and twin.moment_format == "packed"
+        assert twin.max_grad_norm == 2.0
+        assert twin._native is None and twin._fast is None and twin._plan_key is None
+        assert twin.mode == _lib.MODE_PACKED
+        assert twin.param_groups[0]["lr"] == 1e-3
