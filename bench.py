@@ -83,6 +83,8 @@ def parse_args():
                     help="N>1 peer/nvls: CTAs per SM of the fused kernel (0: one per tile)")
     ap.add_argument("--bucket-elems", type=int, default=None,
                     help="N>1: elements per pipelined bucket (default: ShardedDFCAdamW's)")
+    ap.add_argument("--overlap-buckets", action="store_true",
+                    help="N>1 peer/nvls: fused kernels of neighbouring buckets on two streams")
     ap.add_argument("--side-priority", type=int, default=None,
                     help="N>1 peer/nvls: CUDA priority of the fused kernel's stream "
                          "(lower is higher; default: ShardedDFCAdamW's)")
@@ -906,6 +908,7 @@ def run_sharded(args, rank, world, device):
                           compress_ctas_per_sm=args.compress_ctas,
                           **({} if args.side_priority is None else
                              {"side_stream_priority": args.side_priority}),
+                          **({"overlap_buckets": True} if args.overlap_buckets else {}),
                           **({} if args.bucket_elems is None else
                              {"bucket_elems": args.bucket_elems}))
     del param
@@ -974,6 +977,7 @@ def run_sharded(args, rank, world, device):
                 "bucket_elems": opt.bucket, "buckets": opt.n_buckets,
                 "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
                 "side_stream_priority": opt.side_stream_priority,
+                "overlap_buckets": opt.overlap_buckets,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
                 "timed_region": "CUDA events on the launching stream; e0 queued behind one "
                                 "untimed in-flight step; max over ranks",

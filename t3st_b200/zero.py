@@ -127,6 +127,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     CUDA priority of the stream that runs the barriers and the
                     fused kernel (lower is higher; PyTorch clamps to the
                     device's range)
+    overlap_buckets peer/nvls: alternate the fused kernels of neighbouring
+                    buckets between two streams, so bucket b's broadcast
+                    overlaps bucket b+1's reduction (the barriers stay in
+                    order on every rank)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -137,7 +141,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  bucket_elems: int = DEFAULT_BUCKET, transport: str = "auto",
                  barrier_timeout_s: float = 30.0, backend=None,
                  fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None,
-                 side_stream_priority: int = 0):
+                 side_stream_priority: int = 0, overlap_buckets: bool = False):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -162,6 +166,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             raise ValueError("the peer and nvls transports reduce bf16 compressed gradients")
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
         self.side_stream_priority = int(side_stream_priority)
+        self.overlap_buckets = bool(overlap_buckets)
         # Peer and nvls transports: the fused kernel of bucket b and the
         # compression of bucket b+1 run on two streams.  The compression grid
         # is capped so that the fused kernel finds room on every SM beside it;
@@ -331,6 +336,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                      v.data_ptr(), 0, 0) for p, _, m, v in group_segs]
             self._peer_segs.append(np.array(segs, dtype=_lib.PEERSEG_DTYPE))
         self._side = torch.cuda.Stream(self.device, priority=self.side_stream_priority)
+        self._sides = [self._side]
+        if self.overlap_buckets:
+            self._sides.append(torch.cuda.Stream(self.device, priority=self.side_stream_priority))
 
     def _barrier(self, stream):
         self._epoch += 1
@@ -363,16 +371,23 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         memory, and the next step() raises."""
         self._check_peer_error()
         main = torch.cuda.current_stream(self.device)
-        side = self._side
+        sides = self._sides
         hyp = kernels.hypers(rows)
         lib = _lib.lib()
-        side.wait_stream(main)
+        for side in sides:
+            side.wait_stream(main)
+        barrier_done = None  # with two side streams, each barrier waits for the previous one
         with torch.cuda.device(self.device):
             for b in range(self.n_buckets):
                 self.kernels.compress_ef(self._bucket(self.flat_grad, b), self._bucket(self.comp, b),
                                          self._bucket(self.resid, b))
+                side = sides[b % len(sides)]
                 side.wait_stream(main)
+                if barrier_done is not None:
+                    side.wait_event(barrier_done)
                 self._barrier(side.cuda_stream)
+                if len(sides) > 1:
+                    barrier_done = side.record_event()
                 segs = self._peer_segs[b]
                 if len(segs):
                     segs["hyper"] = index[b]
@@ -381,11 +396,14 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                         self._param_mc, self.world, self.rank, _lib.ptr(segs), len(segs),
                         _lib.ptr(hyp), len(rows), self.mode, None, self.peer_error.data_ptr(),
                         self.fused_ctas, side.cuda_stream))
-            self._barrier(side.cuda_stream)
-            with torch.cuda.stream(side):
+            last = sides[0]
+            for side in sides[1:]:
+                last.wait_stream(side)
+            self._barrier(last.cuda_stream)
+            with torch.cuda.stream(last):
                 self._peer_error_host.copy_(self.peer_error, non_blocking=True)
-                self._peer_error_copied = side.record_event()
-        main.wait_stream(side)
+                self._peer_error_copied = last.record_event()
+        main.wait_stream(last)
 
     def peer_status(self) -> int:
         """0, or 1 + the rank a barrier gave up waiting for (synchronises)."""

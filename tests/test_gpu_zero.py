@@ -49,7 +49,7 @@ def _check_switch_sums(opt, red, world):
 
 
 def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=8192,
-         fused_ctas=None):
+         fused_ctas=None, overlap=False):
     from t3st_b200.zero import ShardedDFCAdamW
 
     torch.manual_seed(0)
@@ -58,7 +58,7 @@ def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=
     p0 = [p.detach().cpu().numpy().reshape(-1).copy() for p in params]
     opt = ShardedDFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed",
                           compress_grads=compress, bucket_elems=bucket, transport=transport,
-                          fused_ctas_per_sm=fused_ctas)
+                          fused_ctas_per_sm=fused_ctas, overlap_buckets=overlap)
     sim_p = [x.copy() for x in p0]
     sim_m = [np.zeros(n, np.uint32) for n in sizes]
     sim_v = [np.zeros(n, np.uint32) for n in sizes]
@@ -259,6 +259,17 @@ def test_fused_kernel_walks_tiles_on_two_gpus(transport):
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
     _spawn(2, transport, shapes=SHAPES_LARGE, bucket=1 << 22, fused_ctas=1)
+
+
+@pytest.mark.parametrize("transport", ["peer", "nvls"])
+def test_overlapped_buckets_on_two_gpus(transport):
+    """Fused kernels of neighbouring buckets on two streams (barriers kept in
+    order): still bit-exact, over several buckets."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if transport == "nvls" and not _multicast_ok():
+        pytest.skip("no NVLink multicast on this node")
+    _spawn(2, transport, overlap=True)
 
 
 @pytest.mark.parametrize("world", [4, 8])
