@@ -154,11 +154,13 @@ class DFCAdamW(torch.optim.Optimizer):
                   max_grad_norm=self.max_grad_norm)
         return st
 
+    # load_state_dict goes through __setstate__ too, with state and
+    # param_groups only: options missing from `state` keep their current values
     def __setstate__(self, state):
         state = dict(state)
-        self.enable_fiber = bool(state.pop("enable_fiber", True))
-        self.moment_format = state.pop("moment_format", "fp32")
-        self.max_grad_norm = state.pop("max_grad_norm", None)
+        self.enable_fiber = bool(state.pop("enable_fiber", getattr(self, "enable_fiber", True)))
+        self.moment_format = state.pop("moment_format", getattr(self, "moment_format", "fp32"))
+        self.max_grad_norm = state.pop("max_grad_norm", getattr(self, "max_grad_norm", None))
         super().__setstate__(state)
         self._plan_key = self._plan = self._fast = self._native = None
 

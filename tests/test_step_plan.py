@@ -86,3 +86,14 @@ def test_copy_and_pickle_keep_format_and_drop_plans():
         assert twin._native is None and twin._fast is None and twin._plan_key is None
         assert twin.mode == _lib.MODE_PACKED
         assert twin.param_groups[0]["lr"] == 1e-3
+
+
+def test_load_state_dict_keeps_format_and_options():
+    """torch.optim.Optimizer.load_state_dict re-enters __setstate__ with state
+    and param_groups only; the optimizer's own format and options stay."""
+    params = [torch.nn.Parameter(torch.zeros(3))]
+    opt = DFCAdamW(params, lr=1e-3, enable_fiber=False, moment_format="packed",
+                   max_grad_norm=2.0)
+    opt.load_state_dict(opt.state_dict())  # same format: no conversion needed
+    assert opt.moment_format == "packed" and opt.enable_fiber is False
+    assert opt.max_grad_norm == 2.0 and opt.mode == _lib.MODE_PACKED
