@@ -470,6 +470,7 @@ def run_single(args, device):
     }
 
     line["reference_default_format"] = run_fp32_format(args, device, peak)
+    line["bf16_params"] = run_lowp_params(args, device, peak)
     if not args.no_sharded_1gpu:
         line["sharded_1gpu"] = run_sharded_1gpu(device, peak, peak_kind)
     if not args.no_host_overhead:
@@ -554,6 +555,42 @@ def run_replay(device, peak, peak_kind, n=REPLAY_BATCH, cpu=True, reps=10):
                                "kind": "port",
                                "sample": f"{k} records through the numpy + zlib codec"}
     return res
+
+
+def run_lowp_params(args, device, peak, dtype=torch.bfloat16, K=300):
+    """The same 62-tensor step with 16-bit parameters and gradients (the
+    reference's bf16/fp16 parameter support, remote/torch_fiber.py:45, 83,
+    114-116): packed moments stay FP32 words, so an update moves 22 bytes
+    (p r+w 4, g 2, m r+w 8, v r+w 8).  Timed like the headline line."""
+    from t3st_b200 import DFCAdamW
+    from t3st_b200.workloads import resnet18_cifar_shapes
+
+    gen = torch.Generator(device=device).manual_seed(2)
+    shapes = resnet18_cifar_shapes()
+    params = [torch.nn.Parameter(torch.empty(s, device=device).normal_(0.0, 0.02, generator=gen)
+                                 .to(dtype)) for s in shapes]
+    for p in params:
+        p.grad = torch.empty(p.shape, device=device).normal_(0.0, 1e-3, generator=gen).to(dtype)
+    n_params = sum(p.numel() for p in params)
+    opt = DFCAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, moment_format="packed")
+    for _ in range(10 + max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(LEAD_IN_STEPS):
+        opt.step()
+    e0.record(stream)
+    for _ in range(K):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    gbs = 22 * n_params / (ms / 1e3) / 1e9
+    return {"param_dtype": str(dtype).replace("torch.", ""), "moment_format": "packed",
+            "value": n_params / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": K,
+            "algorithmic_bytes_per_param": 22, "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / peak,
+            "kernel": "dfc::step_kernel<PACKED, bf16 grad, bf16 param>"}
 
 
 def run_fp32_format(args, device, peak, K=300):

@@ -10,6 +10,7 @@
 // Packed words: decoded before and re-encoded after with integer bit ops.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "dfc_common.cuh"
@@ -17,11 +18,12 @@
 namespace dfc {
 
 // ---- 16-bit parameter types ----------------------------------------------
-// Round to nearest even; a NaN becomes the type's canonical quiet NaN (bf16
-// 0x7FC0, fp16 0x7E00), as PyTorch's CPU conversions produce.
+// Round to nearest even with the hardware conversions (cvt.rn.bf16.f32 /
+// cvt.rn.f16.f32; subnormals kept, -ftz=false); a NaN that is stored becomes
+// the type's canonical quiet NaN (bf16 0x7FC0, fp16 0x7E00), as PyTorch's CPU
+// conversions produce.
 __device__ __forceinline__ uint32_t f32_to_bf16_bits(float x) {
-  const uint32_t b = f2u(x);
-  return (b & 0x7FFFFFFFu) > 0x7F800000u ? 0x7FC0u : (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
+  return x != x ? 0x7FC0u : static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
 }
 
 __device__ __forceinline__ uint32_t f32_to_f16_bits(float x) {
@@ -38,10 +40,14 @@ __device__ __forceinline__ float from_bits16(uint32_t h) {
   return DT == DFC_DTYPE_BF16 ? u2f(h << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
 }
 
-// x rounded to the parameter type (identity for FP32)
+// x rounded to the parameter type (identity for FP32), as an intermediate
+// value: a NaN stays a NaN (which one does not matter: every NaN that reaches
+// a stored parameter is canonicalised by to_bits16).
 template <int DT>
 __device__ __forceinline__ float round_to(float x) {
-  return DT == DFC_DTYPE_F32 ? x : from_bits16<DT>(to_bits16<DT>(x));
+  if (DT == DFC_DTYPE_F32) return x;
+  if (DT == DFC_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return __half2float(__float2half_rn(x));
 }
 
 struct Scalars {

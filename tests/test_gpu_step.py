@@ -270,3 +270,54 @@ def test_parameter_and_gradient_types(cuda, pdt, gdt, mode):
         np.testing.assert_array_equal(got_p.view(p.dtype), p)
         np.testing.assert_array_equal(tm.cpu().numpy().view(np.uint32), m)
         np.testing.assert_array_equal(tv.cpu().numpy().view(np.uint32), v)
+
+
+@pytest.mark.parametrize("pdt", ["bf16", "f16"])
+@pytest.mark.parametrize("mode", [O.MODE_SIGNFIBER, O.MODE_PACKED])
+def test_every_16bit_parameter_pattern(cuda, pdt, mode):
+    """Every 16-bit parameter bit pattern (normals, subnormals, +-0, +-Inf,
+    NaNs), four times each, against gradients spread over a wide range of
+    exponents (with zeros, Inf and NaN mixed in), a decay that is not a power
+    of two and a large step size, so that the roundings to the parameter type
+    -- of p * decay, of m, of the denominator and of the new parameter --
+    meet subnormal, overflowing and NaN results; bit for bit against the
+    oracle (round to nearest even, canonical NaN as PyTorch's CPU
+    conversions give)."""
+    rng = np.random.default_rng(100 + mode + (pdt == "f16"))
+    p = np.tile(np.arange(65536, dtype=np.uint32).astype(np.uint16), 4)
+    n = p.size
+    sign = rng.integers(0, 2, n, dtype=np.uint32) << 31
+    expo = rng.integers(0x30, 0x4C, n, dtype=np.uint32) << 23
+    g = (sign | expo | rng.integers(0, 1 << 23, n, dtype=np.uint32)).view(np.float32)
+    g[rng.integers(0, n, 64)] = 0.0
+    g[rng.integers(0, n, 16)] = np.inf
+    g[rng.integers(0, n, 16)] = np.nan
+    m = (rng.standard_normal(n) * 1e-2).astype(np.float32).view(np.uint32)
+    v = (np.abs(rng.standard_normal(n)) * 1e-3).astype(np.float32).view(np.uint32)
+    v |= rng.integers(0, 2, n, dtype=np.uint32) << 31
+    if mode == O.MODE_PACKED:
+        m = O.pack_first(m.view(np.float32))
+        v = O.pack_second(v)
+    h = O.reference_hyper(0.5, (0.9, 0.999), 1e-8, 0.6, 3)
+    tp = torch.from_numpy(p.view(np.int16).copy()).to(cuda).view(NPDT[pdt][1])
+    tg = torch.from_numpy(g.copy()).to(cuda)
+    tm = torch.from_numpy(m.view(np.int32).copy()).to(cuda)
+    tv = torch.from_numpy(v.view(np.int32).copy()).to(cuda)
+    codes = {"bf16": _lib.DTYPE_BF16, "f16": _lib.DTYPE_F16}
+    segs = np.zeros(1, dtype=_lib.SEGMENT_DTYPE)
+    segs[0] = (tp.data_ptr(), tg.data_ptr(), tm.data_ptr(), tv.data_ptr(), n, 0, _lib.DTYPE_F32,
+               codes[pdt])
+    kernels.mt_step_raw(segs, kernels.hypers([_row_tuple(h)]), mode, cuda)
+    torch.cuda.synchronize()
+    O.step(mode, h, p, g, m, v, param_dtype=pdt, grad_dtype="f32")
+    # parameters: bit for bit, NaNs canonical
+    np.testing.assert_array_equal(tp.cpu().view(torch.int16).numpy().view(np.uint16), p)
+    got_m = tm.cpu().numpy().view(np.uint32)
+    got_v = tv.cpu().numpy().view(np.uint32)
+    if mode == O.MODE_PACKED:  # packed words store the canonical NaN: bit for bit
+        np.testing.assert_array_equal(got_m, m)
+        np.testing.assert_array_equal(got_v, v)
+    else:  # FP32 words keep the arithmetic's NaN, whose payload differs by machine
+        assert _same(got_m, m)
+        assert _same(got_v & 0x7FFFFFFF, v & 0x7FFFFFFF)
+        np.testing.assert_array_equal(got_v >> 31, v >> 31)  # payload bits
