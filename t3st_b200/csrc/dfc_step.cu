@@ -51,7 +51,33 @@ namespace {
 constexpr int kThreads = DFC_STEP_THREADS;
 constexpr int kVec = 4;
 constexpr int kUnroll = DFC_STEP_UNROLL;
-constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA
+constexpr int kTile = kThreads * kVec * kUnroll;  // elements per CTA, FP32 parameters
+// 16-bit parameters move fewer bytes per element (22 instead of 28), so a
+// thread takes two quads per stream to keep as many bytes in flight: 2 quads
+// at 5 CTAs per SM (48 registers, no spill) measured 275 G param-updates/s on
+// the bf16 ResNet-18 step, 1 quad at 8 CTAs per SM 262, 2 quads at 4 CTAs 259
+#ifndef DFC_STEP_UNROLL_16
+#define DFC_STEP_UNROLL_16 2
+#endif
+#ifndef DFC_STEP_MIN_BLOCKS_16
+#define DFC_STEP_MIN_BLOCKS_16 5
+#endif
+template <int PDT>
+__host__ __device__ constexpr int unroll_of() { return PDT == DFC_DTYPE_F32 ? kUnroll : DFC_STEP_UNROLL_16; }
+template <int PDT>
+__host__ __device__ constexpr int tile_of() { return kThreads * kVec * unroll_of<PDT>(); }
+int tile_elems(int32_t param_dtype) {
+  return param_dtype == DFC_DTYPE_F32 ? kTile : kThreads * kVec * DFC_STEP_UNROLL_16;
+}
+// resident CTAs per SM asked of a kernel: packed FP32 parameters, FP32 words,
+// or 16-bit parameters (default: as the moment format asks)
+template <int MODE, int PDT>
+__host__ __device__ constexpr int min_blocks_of() {
+#ifdef DFC_STEP_MIN_BLOCKS_16
+  if (PDT != DFC_DTYPE_F32) return DFC_STEP_MIN_BLOCKS_16;
+#endif
+  return MODE == DFC_MODE_PACKED ? DFC_STEP_MIN_BLOCKS : DFC_STEP_MIN_BLOCKS_FP32;
+}
 
 // SegArg.flags: bit 0 = the four-element vector path is aligned.
 constexpr int32_t kFlagVec = 1;
@@ -124,10 +150,11 @@ __device__ __forceinline__ void step4(const Scalars& s, float4& P, const float4&
 
 template <int MODE, int GDT, int PDT>
 __device__ __forceinline__ void tile_full_vec(const SegArg& sg, int64_t base, const Scalars& s) {
-  float4 P[kUnroll], G[kUnroll];
-  uint4 M[kUnroll], V[kUnroll];
+  constexpr int U = unroll_of<PDT>();
+  float4 P[U], G[U];
+  uint4 M[U], V[U];
 #pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
     P[u] = load4<PDT>(sg.p, i);
     G[u] = load4<GDT>(sg.g, i);
@@ -135,7 +162,7 @@ __device__ __forceinline__ void tile_full_vec(const SegArg& sg, int64_t base, co
     V[u] = __ldcs(reinterpret_cast<const uint4*>(sg.v + i));
   }
 #pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int64_t i = base + static_cast<int64_t>(u * kThreads + threadIdx.x) * kVec;
     step4<MODE, PDT>(s, P[u], G[u], M[u], V[u]);
     store4<PDT>(sg.p, i, P[u]);
@@ -178,7 +205,7 @@ template <int MODE, int GDT, int PDT>
 __device__ __forceinline__ void run_tile(const SegArg& sg, int64_t base, int64_t count,
                                          const Scalars& s) {
   const bool vec = (sg.flags & kFlagVec) != 0;
-  if (vec && count == kTile) tile_full_vec<MODE, GDT, PDT>(sg, base, s);
+  if (vec && count == tile_of<PDT>()) tile_full_vec<MODE, GDT, PDT>(sg, base, s);
   else tile_partial<MODE, GDT, PDT>(sg, base, count, vec, s);
 }
 
@@ -186,8 +213,7 @@ __device__ __forceinline__ void run_tile(const SegArg& sg, int64_t base, int64_t
 // holds segments of a single type combination, so the hot FP32 kernel keeps
 // its 32-register budget.
 template <int MODE, int GDT, int PDT, int MAXS, int MAXH>
-__global__ void __launch_bounds__(kThreads, MODE == DFC_MODE_PACKED ? DFC_STEP_MIN_BLOCKS
-                                                                  : DFC_STEP_MIN_BLOCKS_FP32)
+__global__ void __launch_bounds__(kThreads, (min_blocks_of<MODE, PDT>()))
     step_kernel(const __grid_constant__ StepBatch<MAXS, MAXH> b) {
   // Programmatic dependent launch: the next step's grid may start once every
   // CTA of this one has started, and waits (griddepcontrol.wait) for this
@@ -203,8 +229,8 @@ __global__ void __launch_bounds__(kThreads, MODE == DFC_MODE_PACKED ? DFC_STEP_M
   asm volatile("griddepcontrol.wait;" ::: "memory");  // before the first global access
   const SegArg& sg = b.seg[lo];
   const Scalars s = load_scalars(b.hyper[sg.hyper], b.dev_scale);
-  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * kTile;
-  const int64_t count = min(static_cast<int64_t>(kTile), sg.n - base);
+  const int64_t base = static_cast<int64_t>(t - b.tile_base[lo]) * tile_of<PDT>();
+  const int64_t count = min(static_cast<int64_t>(tile_of<PDT>()), sg.n - base);
   run_tile<MODE, GDT, PDT>(sg, base, count, s);
 }
 
@@ -315,7 +341,8 @@ int run_batches(const DfcSegment* segs, int32_t n, const DfcHyper* hypers, int32
   for (int32_t i = 0; i < n; ++i) {
     const DfcSegment& s = segs[i];
     if (s.numel == 0 || types_of(s) != types) continue;
-    const int32_t tiles = static_cast<int32_t>((s.numel + kTile - 1) / kTile);
+    const int64_t tile = tile_elems(s.param_dtype);
+    const int32_t tiles = static_cast<int32_t>((s.numel + tile - 1) / tile);
     const bool need_hyper = local[s.hyper] < 0;
     if (b.n_segs == MAXS || (need_hyper && static_cast<int>(used.size()) == MAXH) ||
         b.tile_base[b.n_segs] > INT32_MAX - tiles) {
