@@ -237,6 +237,14 @@ class DFCAdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        plan = self._native  # steps under hooks or a profiler keep the native plan
+        if plan is not None:
+            rc = plan.step()
+            if rc == 1:
+                return loss
+            self._native = None
+            if rc < 0:
+                _lib.check("dfc_mt_step", rc)
         fast = self._fast
         if fast is not None and fast.try_step(self):
             return loss

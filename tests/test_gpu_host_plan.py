@@ -56,13 +56,14 @@ def test_native_plan_steps_match_oracle(cuda, fmt, fiber, mode):
         grads = [(torch.randn(s, generator=gen) * 1e-3).to(dt) for s, dt in zip(SHAPES, DTYPES)]
         for p, g in zip(params, grads):
             p.grad = g.to(cuda)  # a new gradient tensor every step
-        native = opt._native is not None
+        plan_before = opt._native
         handle = opt.register_step_pre_hook(lambda o, a, k: seen.append(step)) if step == 5 else None
         opt.step()
         if handle is not None:
             handle.remove()
-        if step >= 2 and step != 5:
-            assert native, f"step {step} did not go through the native plan"
+        if step >= 2:  # the same plan every step, the hooked step (5) included
+            assert plan_before is not None and opt._native is plan_before, \
+                f"step {step} left the native plan"
         torch.cuda.synchronize()
         h = O.reference_hyper(lr, betas, eps, wd, step)
         for i, (p, g) in enumerate(zip(params, grads)):
