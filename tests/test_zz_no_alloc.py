@@ -7,7 +7,8 @@ library, so the caller passes only the gradients and the output records.
 The test calls it through the C ABI twice in a row, on different inputs, and
 checks each result against the allocating entry point dfc_grad_stats with the
 tolerance the other statistics tests use (sum of squares to 1e-12 relative,
-max and non-finite count exact).  This file is collected last so that a run
+max and non-finite count exact), and against the CPU oracle's statistics of
+the same values.  This file is collected last so that a run
 stopping at the first failure has already run every other test; it also
 passes alone in a fresh process."""
 
@@ -54,12 +55,26 @@ def _check(got, want):
             assert a == pytest.approx(b, rel=1e-12, abs=0)
 
 
+def _check_oracle(got, grads):
+    """Also against the CPU oracle's statistics of the same values."""
+    from oracle import oracle as O
+
+    for rec, g in zip(got, grads):
+        s, a, bad = O.grad_stats(g.float().cpu().numpy())
+        assert rec["nonfinite"] == bad and rec["amax"] == np.float32(a)
+        if np.isnan(s):
+            assert np.isnan(rec["sumsq"])
+        else:
+            assert rec["sumsq"] == pytest.approx(s, rel=1e-12, abs=0)
+
+
 def test_noalloc_stats_match_the_scratch_entry_point_on_two_calls(cuda):
     for seed in (1, 2):  # two calls in a row on different inputs
         grads = _inputs(cuda, seed)
         want = kernels.stats_to_numpy(kernels.grad_stats(grads))
         got = _noalloc(grads, cuda)
         _check(got, want)
+        _check_oracle(got, grads)
 
 
 def test_noalloc_rejects_requests_beyond_the_static_capacity(cuda):
