@@ -14,6 +14,9 @@ without a host round trip.
 
 from __future__ import annotations
 
+import bisect
+import struct
+
 import numpy as np
 import torch
 
@@ -21,6 +24,8 @@ from . import _lib
 
 RECORD_BYTES = _lib.REPLAY_RECORD_BYTES
 PIXELS = _lib.REPLAY_PIXELS
+# reservoir header: magic, records held (uint32), records offered (uint64)
+_RESERVOIR_HEADER = struct.Struct("<4sIQ")
 
 
 def _device_of(t: torch.Tensor | None) -> torch.device:
@@ -187,92 +192,106 @@ def _has_device_io(channel) -> bool:
 
 
 class CompositeChannel:
-    """Channels joined end to end (vision_benchmark.py:41-71)."""
+    """Channels joined end to end into one byte space (the benchmark's
+    CompositeChannel, vision_benchmark.py:41-71: same capacity, same
+    ``IndexError("channel range out of bounds")``, channels of zero capacity
+    never addressed).  A byte range is cut into per-channel pieces by a
+    binary search over the channels' start offsets; the device forms move
+    each piece with the channel's own device I/O where it has one."""
 
     def __init__(self, channels):
         self.channels = tuple(channels)
-        self.ends = np.cumsum([channel.byte_capacity for channel in channels], dtype=np.int64)
+        sizes = [int(c.byte_capacity) for c in self.channels]
+        self._starts = [0] * len(sizes)
+        for i in range(1, len(sizes)):
+            self._starts[i] = self._starts[i - 1] + sizes[i - 1]
+        self._stops = [a + n for a, n in zip(self._starts, sizes)]
+        self._total = self._stops[-1] if sizes else 0
 
     @property
     def byte_capacity(self) -> int:
-        return int(self.ends[-1])
+        return self._total
 
-    def _segments(self, start: int, count: int):
-        if start < 0 or count < 0 or start + count > self.byte_capacity:
+    def _pieces(self, start: int, count: int) -> list:
+        """[(channel, offset in it, length)] covering [start, start + count)."""
+        start, count = int(start), int(count)
+        stop = start + count
+        if start < 0 or count < 0 or stop > self._total:
             raise IndexError("channel range out of bounds")
-        position, remaining = int(start), int(count)
-        while remaining:
-            index = int(np.searchsorted(self.ends, position, side="right"))
-            base = 0 if index == 0 else int(self.ends[index - 1])
-            local = position - base
-            take = min(remaining, self.channels[index].byte_capacity - local)
-            yield self.channels[index], local, take
-            position += take
-            remaining -= take
+        pieces = []
+        # the last channel that begins at or before ``start``: a zero-capacity
+        # channel sharing that offset comes earlier and is passed over
+        i = bisect.bisect_right(self._starts, start) - 1
+        while start < stop:
+            if self._stops[i] > start:
+                n = min(stop, self._stops[i]) - start
+                pieces.append((self.channels[i], start - self._starts[i], n))
+                start += n
+            i += 1
+        return pieces
 
     def read_bytes(self, start: int, count: int) -> bytes:
-        return b"".join(c.read_bytes(local, take) for c, local, take in self._segments(start, count))
+        return b"".join(c.read_bytes(at, n) for c, at, n in self._pieces(start, count))
 
     def write_bytes(self, start: int, payload) -> None:
-        raw, cursor = bytes(payload), 0
-        for channel, local, take in self._segments(start, len(raw)):
-            channel.write_bytes(local, raw[cursor:cursor + take])
-            cursor += take
+        data = bytes(payload)
+        done = 0
+        for c, at, n in self._pieces(start, len(data)):
+            c.write_bytes(at, data[done:done + n])
+            done += n
 
     @property
     def device_io(self) -> bool:
         return all(_has_device_io(c) for c in self.channels)
 
     def read_device(self, start: int, count: int, device=None) -> torch.Tensor:
-        parts = []
-        for channel, local, take in self._segments(start, count):
-            if _has_device_io(channel):
-                parts.append(channel.read_device(local, take))
-            else:
-                raw = channel.read_bytes(local, take)
-                parts.append(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
         dev = torch.device(device) if device is not None else _device_of(None)
-        if not parts:
-            return torch.empty(0, dtype=torch.uint8, device=dev)
-        return torch.cat([p.to(dev) for p in parts])
+        parts = []
+        for c, at, n in self._pieces(start, count):
+            if _has_device_io(c):
+                parts.append(c.read_device(at, n).to(dev))
+            else:
+                parts.append(torch.frombuffer(bytearray(c.read_bytes(at, n)),
+                                              dtype=torch.uint8).to(dev))
+        if len(parts) == 1:
+            return parts[0]
+        return torch.cat(parts) if parts else torch.empty(0, dtype=torch.uint8, device=dev)
 
     def write_device(self, start: int, data: torch.Tensor) -> None:
-        flat, cursor = data.reshape(-1), 0
-        for channel, local, take in self._segments(start, flat.numel()):
-            piece = flat[cursor:cursor + take]
-            if _has_device_io(channel):
-                channel.write_device(local, piece)
+        flat = data.reshape(-1)
+        done = 0
+        for c, at, n in self._pieces(start, flat.numel()):
+            if _has_device_io(c):
+                c.write_device(at, flat[done:done + n])
             else:
-                channel.write_bytes(local, piece.cpu().numpy().tobytes())
-            cursor += take
+                c.write_bytes(at, flat[done:done + n].cpu().numpy().tobytes())
+            done += n
 
 
 # ---- reservoir ----------------------------------------------------------------
 class FiberReservoir:
     """Reservoir of replay records in a byte channel
     (vision_benchmark.py:103-151): a 16-byte header ("CVR2", size uint32,
-    seen uint64) and then fixed 1552-byte slots.  Same slot choice and the
-    same draws from ``rng`` as the reference, so the channel ends up holding
-    the same bytes."""
+    seen uint64, little-endian) and then fixed 1552-byte slots.  Same slot
+    choice and the same draws from ``rng`` as the reference, so the channel
+    ends up holding the same bytes."""
 
-    HEADER_BYTES = 16
+    HEADER_BYTES = _RESERVOIR_HEADER.size
     MAGIC = b"CVR2"
 
     def __init__(self, channel):
         self.channel = channel
-        self.capacity = max(0, (channel.byte_capacity - self.HEADER_BYTES) // RECORD_BYTES)
-        raw = channel.read_bytes(0, min(self.HEADER_BYTES, channel.byte_capacity))
-        if len(raw) == self.HEADER_BYTES and raw[:4] == self.MAGIC:
-            self.size = int.from_bytes(raw[4:8], "little")
-            self.seen = int.from_bytes(raw[8:16], "little")
-        else:
-            self.size = self.seen = 0
-            if channel.byte_capacity >= self.HEADER_BYTES:
-                self._header()
+        room = channel.byte_capacity
+        self.capacity = max(0, (room - self.HEADER_BYTES) // RECORD_BYTES)
+        self.size = self.seen = 0
+        head = channel.read_bytes(0, min(self.HEADER_BYTES, room))
+        if len(head) == self.HEADER_BYTES and head[:4] == self.MAGIC:
+            _, self.size, self.seen = _RESERVOIR_HEADER.unpack(head)  # resume
+        elif room >= self.HEADER_BYTES:
+            self._header()  # a fresh reservoir stamps its empty header
 
     def _header(self) -> None:
-        self.channel.write_bytes(
-            0, self.MAGIC + self.size.to_bytes(4, "little") + self.seen.to_bytes(8, "little"))
+        self.channel.write_bytes(0, _RESERVOIR_HEADER.pack(self.MAGIC, self.size, self.seen))
 
     def _offset(self, index: int) -> int:
         return self.HEADER_BYTES + index * RECORD_BYTES

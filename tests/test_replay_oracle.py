@@ -107,6 +107,55 @@ def test_mirror_composite_channel_bounds():
         c.read_bytes(10, 3)
 
 
+def test_composite_channel_matches_one_flat_store():
+    """Random reads and writes through a composite with zero-capacity members
+    (first, middle and last) behave as one flat byte store of the summed
+    capacity; zero-capacity members are never called; ranges outside it
+    raise the benchmark's IndexError (vision_benchmark.py:41-71)."""
+    from t3st_b200.replay import ArrayChannel, CompositeChannel
+
+    class Counted(ArrayChannel):
+        def __init__(self, n):
+            super().__init__(n)
+            self.calls = 0
+
+        def read_bytes(self, start, count):
+            self.calls += 1
+            assert 0 <= start and start + count <= self.byte_capacity and count > 0
+            return super().read_bytes(start, count)
+
+        def write_bytes(self, start, payload):
+            self.calls += 1
+            assert isinstance(payload, bytes) and 0 < len(payload)
+            assert start + len(payload) <= self.byte_capacity
+            super().write_bytes(start, payload)
+
+    sizes = [0, 3, 0, 0, 11, 1, 0, 6, 0]
+    parts = [Counted(n) for n in sizes]
+    c = CompositeChannel(parts)
+    flat = bytearray(sum(sizes))
+    assert c.byte_capacity == len(flat) == 21
+    rng = np.random.default_rng(9)
+    for _ in range(400):
+        a = int(rng.integers(0, len(flat) + 1))
+        n = int(rng.integers(0, len(flat) - a + 1))
+        if rng.integers(0, 2):
+            data = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+            c.write_bytes(a, data)
+            flat[a:a + n] = data
+        else:
+            assert c.read_bytes(a, n) == bytes(flat[a:a + n])
+    assert c.read_bytes(0, len(flat)) == bytes(flat)
+    assert all(p.calls == 0 for p, n in zip(parts, sizes) if n == 0)
+    for a, n in [(-1, 1), (0, -1), (21, 1), (20, 2), (0, 22)]:
+        with pytest.raises(IndexError, match="channel range out of bounds"):
+            c.read_bytes(a, n)
+    with pytest.raises(IndexError, match="channel range out of bounds"):
+        c.write_bytes(19, b"abc")
+    assert CompositeChannel([]).byte_capacity == 0
+    assert CompositeChannel([]).read_bytes(0, 0) == b""
+
+
 def _rn32(x):
     """A Fraction rounded to the nearest FP32 value, ties to even."""
     from fractions import Fraction
