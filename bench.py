@@ -85,6 +85,9 @@ def parse_args():
                     help="N>1: elements per pipelined bucket (default: ShardedDFCAdamW's)")
     ap.add_argument("--overlap-buckets", action="store_true",
                     help="N>1 peer/nvls: fused kernels of neighbouring buckets on two streams")
+    ap.add_argument("--fuse-compression", action=argparse.BooleanOptionalAction, default=None,
+                    help="N>1 peer/nvls: compress bucket b+1 inside bucket b's fused kernel "
+                         "(default: ShardedDFCAdamW's)")
     ap.add_argument("--side-priority", type=int, default=None,
                     help="N>1 peer/nvls: CUDA priority of the fused kernel's stream "
                          "(lower is higher; default: ShardedDFCAdamW's)")
@@ -946,6 +949,8 @@ def run_sharded(args, rank, world, device):
                           **({} if args.side_priority is None else
                              {"side_stream_priority": args.side_priority}),
                           **({"overlap_buckets": True} if args.overlap_buckets else {}),
+                          **({} if args.fuse_compression is None else
+                             {"fuse_compression": args.fuse_compression}),
                           **({} if args.bucket_elems is None else
                              {"bucket_elems": args.bucket_elems}))
     del param
@@ -1015,6 +1020,7 @@ def run_sharded(args, rank, world, device):
                 "compress_ctas_per_sm": getattr(opt.kernels, "compress_ctas", None),
                 "side_stream_priority": opt.side_stream_priority,
                 "overlap_buckets": opt.overlap_buckets,
+                "fuse_compression": opt.fuse_compression,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
                 "timed_region": "CUDA events on the launching stream; e0 queued behind one "
                                 "untimed in-flight step; max over ranks",
@@ -1046,8 +1052,12 @@ def run_sharded(args, rank, world, device):
             # this run (the all-gather rate above), as the sharded roofline is defined
             # over the measured NCCL bandwidth; the line above uses 770 GB/s
             "roofline_frac_ratio_vs_1gpu_nccl_rate": (value / roof_rate_ag) / frac_alone,
-            "gpu_launches": K * (3 * opt.n_buckets + 1 if opt.transport in ("peer", "nvls")
-                                 else 2 * opt.n_buckets),
+            # per step: peer/nvls -- a barrier and a fused kernel per bucket, the
+            # closing barrier, and a compression per bucket (fused: only bucket 0's
+            # runs alone); nccl -- a compression and a step per bucket
+            "gpu_launches": K * ((2 * opt.n_buckets + 2 if opt.fuse_compression
+                                  else 3 * opt.n_buckets + 1)
+                                 if opt.transport in ("peer", "nvls") else 2 * opt.n_buckets),
             "clocks": clocks,
         }
     if not args.no_e2e:

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define DFC_ABI_VERSION 2
+#define DFC_ABI_VERSION 3
 
 /* Entry points are the library's only exported symbols (it is built with
  * -fvisibility=hidden). */
@@ -147,6 +147,15 @@ typedef struct DfcPeerSegment {
   int32_t hyper;         /* index into the call's DfcHyper array */
   int32_t reserved;
 } DfcPeerSegment;
+
+/* A gradient range for dfc_compress_ef run inside another launch's grid
+ * (dfc_zero_fused_step_ef).  32 bytes. */
+typedef struct DfcCompressRange {
+  const float* grad;     /* numel FP32 gradients, 16-byte aligned */
+  uint16_t* comp;        /* numel bf16 halves, 8-byte aligned */
+  uint16_t* resid;       /* numel residual halves, 8-byte aligned */
+  int64_t numel;         /* a multiple of 4 */
+} DfcCompressRange;
 
 /* A run of second-moment words whose bit 31 forms part of the sign fiber.
  * words == NULL makes the run a hole of `count` bits that live elsewhere
@@ -319,6 +328,25 @@ DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param
                                 int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                 int32_t mode, const float* device_grad_scale,
                                 const int32_t* error_flag, int32_t ctas_per_sm, void* stream);
+
+/*
+ * dfc_zero_fused_step and dfc_compress_ef(next->grad, next->comp, next->resid,
+ * next->numel) in one launch (no reference counterpart).  The grid's tiles are
+ * the step's and the compression's, spread evenly, so the step's NVLink
+ * traffic and the compression's HBM traffic overlap inside one kernel -- in
+ * the ZeRO-1 pipeline, the compression of bucket b+1 beside the step of
+ * bucket b.  Results are bit for bit those of the two calls.  next's buffers
+ * must not overlap anything the step reads or writes.  The compression runs
+ * even when *error_flag is set (it touches only the memory it is given).
+ * next == NULL or next->numel == 0: dfc_zero_fused_step.
+ */
+DFC_API int dfc_zero_fused_step_ef(const void* const* comp_ptrs, void* const* param_ptrs,
+                                   const void* comp_multicast, void* param_multicast,
+                                   int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
+                                   int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
+                                   int32_t mode, const float* device_grad_scale,
+                                   const int32_t* error_flag, const DfcCompressRange* next,
+                                   int32_t ctas_per_sm, void* stream);
 
 /*
  * The NVSwitch sum over every rank of numel bf16 values at a multicast

@@ -18,7 +18,7 @@ from . import build as _build
 LIB_PATH = _build.LIB_PATH
 
 # ---- status codes / enums (mirror include/dfc_b200.h) ----
-ABI_VERSION = 2
+ABI_VERSION = 3
 DFC_OK = 0
 DFC_ERR_NULL = -1
 DFC_ERR_ALIGN = -2
@@ -61,10 +61,13 @@ GRADSTATS_DTYPE = np.dtype([("sumsq", "<f8"), ("amax", "<f4"), ("reserved", "<i4
 WORDRANGE_DTYPE = np.dtype([("words", "<u8"), ("count", "<i8")])
 PEERSEG_DTYPE = np.dtype([("offset", "<i8"), ("numel", "<i8"), ("exp_avg", "<u8"),
                           ("exp_avg_sq", "<u8"), ("hyper", "<i4"), ("reserved", "<i4")])
+COMPRESSRANGE_DTYPE = np.dtype([("grad", "<u8"), ("comp", "<u8"), ("resid", "<u8"),
+                                ("numel", "<i8")])
 MAX_PEERS = 8
 assert SEGMENT_DTYPE.itemsize == 48 and HYPER_DTYPE.itemsize == 48
 assert GRADREF_DTYPE.itemsize == 24 and GRADSTATS_DTYPE.itemsize == 24
 assert WORDRANGE_DTYPE.itemsize == 16 and PEERSEG_DTYPE.itemsize == 40
+assert COMPRESSRANGE_DTYPE.itemsize == 32
 
 # Names of every entry point the header declares (checked by the CPU tests).
 EXPORTS = (
@@ -72,7 +75,8 @@ EXPORTS = (
     "dfc_pack_moments", "dfc_unpack_moments", "dfc_compress_ef",
     "dfc_grad_stats_scratch_bytes", "dfc_grad_stats", "dfc_clip_coef",
     "dfc_fiber_read", "dfc_fiber_write", "dfc_grad_stats_noalloc",
-    "dfc_zero_fused_step", "dfc_peer_barrier", "dfc_multicast_sum_bf16",
+    "dfc_zero_fused_step", "dfc_zero_fused_step_ef", "dfc_peer_barrier",
+    "dfc_multicast_sum_bf16",
     "dfc_replay_encode", "dfc_replay_decode",
 )
 
@@ -109,6 +113,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
         "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, I32, P],
                                 ctypes.c_int),
+        "dfc_zero_fused_step_ef": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, P, I32, P],
+                                   ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
         "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
         "dfc_replay_encode": ([P, I64, P, P, I64, P, I64, P], ctypes.c_int),

@@ -20,6 +20,11 @@
 // once instead of once per peer.  dfc_multicast_sum_bf16 reads the switch's
 // sums back, for checking.
 //
+// dfc_zero_fused_step_ef adds the next bucket's gradient compression to the
+// same grid: its tiles are spread evenly among the step's, so the step's
+// NVLink traffic and the compression's HBM traffic run side by side in one
+// kernel instead of two kernels on two streams competing for SMs.
+//
 // dfc_peer_barrier orders the ranks around it: each rank writes an epoch to
 // its slot in every peer's signal array (release, system scope) and then
 // waits for every peer's slot in its own array (acquire, system scope), for at
@@ -28,6 +33,7 @@
 #include <vector>
 
 #include "dfc_common.cuh"
+#include "dfc_compress_elem.cuh"
 #include "dfc_step_elem.cuh"
 
 namespace dfc {
@@ -55,6 +61,11 @@ struct ZeroBatch {
   float* param_mc;                  // multicast address of the parameters (nvls kernel)
   const float* dev_scale;
   const int32_t* error;             // a barrier's give-up flag, or null
+  const float* cgrad;               // compression run in the same grid (dfc_zero_fused_step_ef)
+  uint16_t* ccomp;
+  uint16_t* cresid;
+  int64_t cquads;                   // its length in quads
+  int32_t ctiles;                   // its tiles of kTile elements (0: none)
   int32_t n_peers;
   int32_t rank;
   int32_t n_segs;
@@ -207,14 +218,33 @@ __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const Pe
 // CTA c handles tiles c, c + gridDim.x, ...: one tile per CTA when the grid
 // has a CTA per tile, a persistent walk when the grid is capped so that a
 // kernel on another stream (the next bucket's compression) keeps SMs.
+//
+// With a compression in the grid the tiles are T = F step tiles + C
+// compression tiles, and tile t is a step tile exactly when
+// floor((t+1) F / T) > floor(t F / T): step tile floor(t F / T), else
+// compression tile t - floor(t F / T).  Both kinds are spread evenly over the
+// grid, in address order within each kind.
 template <int MODE, int NP, bool NVLS, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, 4)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
   // A barrier before this kernel gave up: a peer may be stalled or gone, so
-  // neither its gradients nor its parameter copy may be touched.
-  if (b.error && *static_cast<const volatile int32_t*>(b.error) != 0) return;
-  const int32_t tiles = b.tile_base[b.n_segs];
-  for (int32_t t = static_cast<int32_t>(blockIdx.x); t < tiles; t += static_cast<int32_t>(gridDim.x)) {
+  // neither its gradients nor its parameter copy may be touched.  The
+  // compression touches this rank's memory only and runs regardless.
+  const bool failed = b.error && *static_cast<const volatile int32_t*>(b.error) != 0;
+  if (failed && b.ctiles == 0) return;
+  const int64_t ftiles = b.tile_base[b.n_segs];
+  const int64_t total = ftiles + b.ctiles;
+  for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
+    int64_t ft = u;
+    if (b.ctiles) {
+      ft = u * ftiles / total;
+      if ((u + 1) * ftiles / total == ft) {
+        compress_tile<kThreads>(b.cgrad, b.ccomp, b.cresid, b.cquads, u - ft);
+        continue;
+      }
+    }
+    if (failed) continue;
+    const int32_t t = static_cast<int32_t>(ft);
     int lo = 0, hi = b.n_segs;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -255,9 +285,10 @@ void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t grid, cudaStream_t st) {
 // One CTA per tile (ctas_per_sm <= 0), or at most ctas_per_sm CTAs per SM.
 template <int MAXS, int MAXH>
 int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, int32_t ctas_per_sm, cudaStream_t st) {
-  const int32_t tiles = b.tile_base[b.n_segs];
+  const int64_t tiles = static_cast<int64_t>(b.tile_base[b.n_segs]) + b.ctiles;
   if (tiles == 0) return DFC_OK;
-  int32_t grid = tiles;
+  if (tiles > INT32_MAX) return DFC_ERR_SIZE;
+  int32_t grid = static_cast<int32_t>(tiles);
   if (ctas_per_sm > 0) grid = static_cast<int32_t>(std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * ctas_per_sm));
   switch (mode) {
     case DFC_MODE_PLAIN: launch_np<DFC_MODE_PLAIN>(b, grid, st); break;
@@ -337,19 +368,30 @@ bool peers_ok(const void* const* ptrs, int32_t n) {
 }  // namespace
 }  // namespace dfc
 
-extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
-                                   const void* comp_multicast, void* param_multicast,
-                                   int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
-                                   int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
-                                   int32_t mode, const float* device_grad_scale,
-                                   const int32_t* error_flag, int32_t ctas_per_sm, void* stream) {
-  using namespace dfc;
+namespace dfc {
+namespace {
+
+int fused_step(const void* const* comp_ptrs, void* const* param_ptrs, const void* comp_multicast,
+               void* param_multicast, int32_t n_peers, int32_t rank,
+               const DfcPeerSegment* segments, int32_t n_segments, const DfcHyper* hypers,
+               int32_t n_hypers, int32_t mode, const float* device_grad_scale,
+               const int32_t* error_flag, const DfcCompressRange* next, int32_t ctas_per_sm,
+               cudaStream_t st) {
   if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers) return DFC_ERR_SIZE;
   if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
   if (mode != DFC_MODE_PLAIN && mode != DFC_MODE_SIGNFIBER && mode != DFC_MODE_PACKED)
     return DFC_ERR_MODE;
-  if (n_segments == 0) return DFC_OK;
-  if (!comp_ptrs || !param_ptrs || !segments || (!hypers && n_hypers > 0)) return DFC_ERR_NULL;
+  const bool compress = next && next->numel != 0;
+  if (compress) {
+    if (next->numel < 0 || next->numel % 4 != 0) return DFC_ERR_SIZE;
+    if (!next->grad || !next->comp || !next->resid) return DFC_ERR_NULL;
+    if (!aligned(next->grad, 16) || !aligned(next->comp, 8) || !aligned(next->resid, 8))
+      return DFC_ERR_ALIGN;
+    if ((next->numel / 4 + 2 * kThreads - 1) / (2 * kThreads) > INT32_MAX / 2) return DFC_ERR_SIZE;
+  }
+  if (n_segments == 0 && !compress) return DFC_OK;
+  if (!comp_ptrs || !param_ptrs || (!segments && n_segments > 0) || (!hypers && n_hypers > 0))
+    return DFC_ERR_NULL;
   if (!peers_ok(comp_ptrs, n_peers) || !peers_ok(param_ptrs, n_peers)) return DFC_ERR_NULL;
   for (int32_t q = 0; q < n_peers; ++q)
     if (!aligned(comp_ptrs[q], 16) || !aligned(param_ptrs[q], 16)) return DFC_ERR_ALIGN;
@@ -376,7 +418,12 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
   b.error = error_flag;
   b.n_peers = n_peers;
   b.rank = rank;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the compression rides with the first launch only
+  b.cgrad = compress ? next->grad : nullptr;
+  b.ccomp = compress ? next->comp : nullptr;
+  b.cresid = compress ? next->resid : nullptr;
+  b.cquads = compress ? next->numel / 4 : 0;
+  b.ctiles = compress ? static_cast<int32_t>((b.cquads + 2 * kThreads - 1) / (2 * kThreads)) : 0;
   std::vector<int32_t> local(static_cast<size_t>(n_hypers), -1);
   std::vector<int32_t> used;
   auto reset = [&]() {
@@ -392,10 +439,11 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     const int32_t tiles = static_cast<int32_t>((s.numel + kTile - 1) / kTile);
     const bool need = local[s.hyper] < 0;
     if (b.n_segs == kMaxSegs || (need && static_cast<int>(used.size()) == kMaxHypers) ||
-        b.tile_base[b.n_segs] > INT32_MAX - tiles) {
+        b.tile_base[b.n_segs] > INT32_MAX / 2 - tiles) {
       const int rc = launch(b, mode, ctas_per_sm, st);
       if (rc != DFC_OK) return rc;
       reset();
+      b.ctiles = 0;
     }
     if (local[s.hyper] < 0) {
       local[s.hyper] = static_cast<int32_t>(used.size());
@@ -412,7 +460,34 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
     b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
     ++b.n_segs;
   }
-  return b.n_segs ? launch(b, mode, ctas_per_sm, st) : DFC_OK;
+  return (b.n_segs || b.ctiles) ? launch(b, mode, ctas_per_sm, st) : DFC_OK;
+}
+
+}  // namespace
+}  // namespace dfc
+
+extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param_ptrs,
+                                   const void* comp_multicast, void* param_multicast,
+                                   int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
+                                   int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
+                                   int32_t mode, const float* device_grad_scale,
+                                   const int32_t* error_flag, int32_t ctas_per_sm, void* stream) {
+  return dfc::fused_step(comp_ptrs, param_ptrs, comp_multicast, param_multicast, n_peers, rank,
+                         segments, n_segments, hypers, n_hypers, mode, device_grad_scale,
+                         error_flag, nullptr, ctas_per_sm, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dfc_zero_fused_step_ef(const void* const* comp_ptrs, void* const* param_ptrs,
+                                      const void* comp_multicast, void* param_multicast,
+                                      int32_t n_peers, int32_t rank,
+                                      const DfcPeerSegment* segments, int32_t n_segments,
+                                      const DfcHyper* hypers, int32_t n_hypers, int32_t mode,
+                                      const float* device_grad_scale, const int32_t* error_flag,
+                                      const DfcCompressRange* next, int32_t ctas_per_sm,
+                                      void* stream) {
+  return dfc::fused_step(comp_ptrs, param_ptrs, comp_multicast, param_multicast, n_peers, rank,
+                         segments, n_segments, hypers, n_hypers, mode, device_grad_scale,
+                         error_flag, next, ctas_per_sm, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64_t numel,

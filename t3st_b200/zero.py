@@ -24,8 +24,11 @@ rank's C(b) done) and one at the end of the step (every rank's parameters
 done) order the ranks, and C(b+1) on the caller's stream overlaps the fused
 kernel of bucket b on a side stream (the compression grid is capped so that
 the two kernels share the SMs).  transport="nvls" is the same kernel with
-the reduction and the broadcast done by the NVSwitch.  Either way the step
-returns with the caller's stream ordered after all of it.
+the reduction and the broadcast done by the NVSwitch.  With
+fuse_compression, C(b+1) runs inside the grid of bucket b's fused kernel
+(dfc_zero_fused_step_ef) rather than as a capped kernel on a second stream:
+one stream, C(0), then a barrier and one kernel per bucket.  Either way the
+step returns with the caller's stream ordered after all of it.
 
 The parameters are re-homed into one flat FP32 buffer (each becomes a view
 of it) and their ``.grad`` into one flat gradient buffer, so the collectives
@@ -131,6 +134,11 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     buckets between two streams, so bucket b's broadcast
                     overlaps bucket b+1's reduction (the barriers stay in
                     order on every rank)
+    fuse_compression
+                    peer/nvls: compress bucket b+1 inside the grid of bucket
+                    b's fused kernel (dfc_zero_fused_step_ef) instead of in a
+                    capped kernel on a second stream; one stream, one kernel
+                    and one barrier per bucket
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -141,7 +149,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  bucket_elems: int = DEFAULT_BUCKET, transport: str = "auto",
                  barrier_timeout_s: float = 30.0, backend=None,
                  fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None,
-                 side_stream_priority: int = 0, overlap_buckets: bool = False):
+                 side_stream_priority: int = 0, overlap_buckets: bool = False,
+                 fuse_compression: bool = False):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -167,6 +176,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
         self.side_stream_priority = int(side_stream_priority)
         self.overlap_buckets = bool(overlap_buckets)
+        self.fuse_compression = bool(fuse_compression)
+        if self.fuse_compression and self.overlap_buckets:
+            raise ValueError("fuse_compression runs every bucket on one stream; "
+                             "overlap_buckets does not apply")
         # Peer and nvls transports: the fused kernel of bucket b and the
         # compression of bucket b+1 run on two streams.  The compression grid
         # is capped so that the fused kernel finds room on every SM beside it;
@@ -337,6 +350,15 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             self._peer_segs.append(np.array(segs, dtype=_lib.PEERSEG_DTYPE))
         self._side = torch.cuda.Stream(self.device, priority=self.side_stream_priority)
         self._sides = [self._side]
+        # fuse_compression: bucket b's kernel compresses bucket b+1 (none after the last)
+        self._next_comp = []
+        for b in range(self.n_buckets):
+            r = np.zeros(1, dtype=_lib.COMPRESSRANGE_DTYPE)
+            if b + 1 < self.n_buckets:
+                r[0] = (self._bucket(self.flat_grad, b + 1).data_ptr(),
+                        self._bucket(self.comp, b + 1).data_ptr(),
+                        self._bucket(self.resid, b + 1).data_ptr(), self.bucket)
+            self._next_comp.append(r)
         if self.overlap_buckets:
             self._sides.append(torch.cuda.Stream(self.device, priority=self.side_stream_priority))
 
@@ -404,6 +426,37 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                 self._peer_error_host.copy_(self.peer_error, non_blocking=True)
                 self._peer_error_copied = last.record_event()
         main.wait_stream(last)
+
+    def _step_peer_fused_compression(self, rows, index):
+        """One stream: C(0) alone (full grid); then for every bucket b a
+        barrier (every rank's C(b) done) and one kernel that steps bucket b
+        and compresses bucket b+1 in the same grid; a last barrier ends the
+        step.  Error handling as in _step_peer (the compression tiles run
+        regardless: they touch only this rank's gradient buffers)."""
+        self._check_peer_error()
+        main = torch.cuda.current_stream(self.device)
+        side = self._sides[0]
+        side.wait_stream(main)
+        hyp = kernels.hypers(rows)
+        lib = _lib.lib()
+        with torch.cuda.device(self.device), torch.cuda.stream(side):
+            kernels.compress_ef(self._bucket(self.flat_grad, 0), self._bucket(self.comp, 0),
+                                self._bucket(self.resid, 0), 0)
+            for b in range(self.n_buckets):
+                self._barrier(side.cuda_stream)
+                segs = self._peer_segs[b]
+                if len(segs):
+                    segs["hyper"] = index[b]
+                _lib.check("dfc_zero_fused_step_ef", lib.dfc_zero_fused_step_ef(
+                    _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self._comp_mc,
+                    self._param_mc, self.world, self.rank, _lib.ptr(segs) if len(segs) else None,
+                    len(segs), _lib.ptr(hyp), len(rows), self.mode, None,
+                    self.peer_error.data_ptr(), _lib.ptr(self._next_comp[b]), self.fused_ctas,
+                    side.cuda_stream))
+            self._barrier(side.cuda_stream)
+            self._peer_error_host.copy_(self.peer_error, non_blocking=True)
+            self._peer_error_copied = side.record_event()
+        main.wait_stream(side)
 
     def peer_status(self) -> int:
         """0, or 1 + the rank a barrier gave up waiting for (synchronises)."""
@@ -520,7 +573,10 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
             index.append(idx)
 
         if self.transport in ("peer", "nvls"):
-            self._step_peer(rows, index)
+            if self.fuse_compression:
+                self._step_peer_fused_compression(rows, index)
+            else:
+                self._step_peer(rows, index)
             return loss
 
         def reduce(b):

@@ -141,6 +141,35 @@ def test_other_entry_points_reject_bad_arguments():
     assert fused(0x70000, rank=2) == _lib.DFC_ERR_SIZE
     segs[0]["hyper"] = 1
     assert fused(0x70000) == _lib.DFC_ERR_HYPER
+    segs[0]["hyper"] = 0
+
+    # the same step with the next bucket's compression in its grid: the
+    # compression range is checked before anything launches
+    nxt = np.zeros(1, dtype=_lib.COMPRESSRANGE_DTYPE)
+
+    def fused_ef(rng, n_segs=1):
+        return lib.dfc_zero_fused_step_ef(comps, params, None, None, 2, 0, _lib.ptr(segs), n_segs,
+                                          _lib.ptr(h), 1, _lib.MODE_PACKED, None, 0x70000,
+                                          None if rng is None else _lib.ptr(rng), 0, None)
+
+    nxt[0] = (0x80000, 0x90000, 0xA0000, 6)
+    assert fused_ef(nxt) == _lib.DFC_ERR_SIZE       # not a whole number of quads
+    nxt[0] = (0x80000, 0x90000, 0xA0000, -4)
+    assert fused_ef(nxt) == _lib.DFC_ERR_SIZE
+    nxt[0] = (0, 0x90000, 0xA0000, 8)
+    assert fused_ef(nxt) == _lib.DFC_ERR_NULL
+    nxt[0] = (0x80008, 0x90000, 0xA0000, 8)
+    assert fused_ef(nxt) == _lib.DFC_ERR_ALIGN      # gradients need 16 bytes
+    nxt[0] = (0x80000, 0x90004, 0xA0000, 8)
+    assert fused_ef(nxt) == _lib.DFC_ERR_ALIGN      # halves need 8
+    nxt[0] = (0x80000, 0x90000, 0xA0000, 8)
+    segs[0]["hyper"] = 1
+    assert fused_ef(nxt) == _lib.DFC_ERR_HYPER      # the step's own checks still apply
+    assert fused_ef(None) == _lib.DFC_ERR_HYPER
+    segs[0]["hyper"] = 0
+    nxt[0] = (0, 0, 0, 0)                            # nothing to compress, no segments: no-op
+    assert fused_ef(nxt, n_segs=0) == _lib.DFC_OK
+    assert fused_ef(None, n_segs=0) == _lib.DFC_OK
 
 
 def test_library_is_self_contained():

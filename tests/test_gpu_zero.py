@@ -49,7 +49,7 @@ def _check_switch_sums(opt, red, world):
 
 
 def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=8192,
-         fused_ctas=None, overlap=False):
+         fused_ctas=None, overlap=False, fuse=False):
     from t3st_b200.zero import ShardedDFCAdamW
 
     torch.manual_seed(0)
@@ -58,7 +58,8 @@ def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=
     p0 = [p.detach().cpu().numpy().reshape(-1).copy() for p in params]
     opt = ShardedDFCAdamW(params, lr=1e-3, weight_decay=0.01, moment_format="packed",
                           compress_grads=compress, bucket_elems=bucket, transport=transport,
-                          fused_ctas_per_sm=fused_ctas, overlap_buckets=overlap)
+                          fused_ctas_per_sm=fused_ctas, overlap_buckets=overlap,
+                          fuse_compression=fuse)
     sim_p = [x.copy() for x in p0]
     sim_m = [np.zeros(n, np.uint32) for n in sizes]
     sim_v = [np.zeros(n, np.uint32) for n in sizes]
@@ -270,6 +271,28 @@ def test_overlapped_buckets_on_two_gpus(transport):
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
     _spawn(2, transport, overlap=True)
+
+
+@pytest.mark.parametrize("transport", ["peer", "nvls"])
+def test_fused_compression_on_two_gpus(transport):
+    """Bucket b+1's compression inside the grid of bucket b's fused kernel
+    (fuse_compression): bit-exact as above over several buckets, with one
+    CTA per tile, and with a capped grid whose CTAs walk step and
+    compression tiles."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if transport == "nvls" and not _multicast_ok():
+        pytest.skip("no NVLink multicast on this node")
+    _spawn(2, transport, fuse=True)
+    _spawn(2, transport, fuse=True, shapes=SHAPES_LARGE, bucket=1 << 20, fused_ctas=1)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_fused_compression_on_more_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    transport = "nvls" if world > 4 and _multicast_ok() else "peer"
+    _spawn(world, transport, fuse=True)
 
 
 @pytest.mark.parametrize("world", [4, 8])

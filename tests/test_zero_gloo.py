@@ -331,3 +331,15 @@ def test_auto_transport_choice():
     assert choose(4, cuda=False) == "nccl"
     if not torch.cuda.is_available():
         assert choose(8) == "peer"
+
+
+def test_fused_compression_excludes_bucket_overlap():
+    """fuse_compression runs every bucket on one stream, so asking for the
+    two-stream bucket overlap as well is refused at construction."""
+    from t3st_b200.zero import ShardedDFCAdamW
+
+    with pytest.raises(ValueError, match="overlap_buckets"):
+        ShardedDFCAdamW([torch.nn.Parameter(torch.zeros(8))], fuse_compression=True,
+                        overlap_buckets=True)
+    opt = ShardedDFCAdamW([torch.nn.Parameter(torch.zeros(8))], fuse_compression=True)
+    assert opt.fuse_compression and opt.transport == "nccl"  # one rank: nothing to fuse into
