@@ -88,6 +88,9 @@ def parse_args():
     ap.add_argument("--fuse-compression", action=argparse.BooleanOptionalAction, default=None,
                     help="N>1 peer/nvls: compress bucket b+1 inside bucket b's fused kernel "
                          "(default: ShardedDFCAdamW's)")
+    ap.add_argument("--overlap-barrier", action=argparse.BooleanOptionalAction, default=None,
+                    help="with --fuse-compression: each bucket's kernel starts its compression "
+                         "while the barrier before it waits (default: ShardedDFCAdamW's)")
     ap.add_argument("--side-priority", type=int, default=None,
                     help="N>1 peer/nvls: CUDA priority of the fused kernel's stream "
                          "(lower is higher; default: ShardedDFCAdamW's)")
@@ -951,6 +954,8 @@ def run_sharded(args, rank, world, device):
                           **({"overlap_buckets": True} if args.overlap_buckets else {}),
                           **({} if args.fuse_compression is None else
                              {"fuse_compression": args.fuse_compression}),
+                          **({} if args.overlap_barrier is None else
+                             {"overlap_barrier": args.overlap_barrier}),
                           **({} if args.bucket_elems is None else
                              {"bucket_elems": args.bucket_elems}))
     del param
@@ -1021,6 +1026,7 @@ def run_sharded(args, rank, world, device):
                 "side_stream_priority": opt.side_stream_priority,
                 "overlap_buckets": opt.overlap_buckets,
                 "fuse_compression": opt.fuse_compression,
+                "overlap_barrier": opt.overlap_barrier,
                 "l2": "inputs 4+ GB per rank per step > 126 MB L2 (no flush)",
                 "timed_region": "CUDA events on the launching stream; e0 queued behind one "
                                 "untimed in-flight step; max over ranks",

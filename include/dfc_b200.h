@@ -339,14 +339,21 @@ DFC_API int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* param
  * must not overlap anything the step reads or writes.  The compression runs
  * even when *error_flag is set (it touches only the memory it is given).
  * next == NULL or next->numel == 0: dfc_zero_fused_step.
+ * flags: 0, or DFC_FUSED_AFTER_BARRIER when the previous operation on the
+ * stream is a dfc_peer_barrier: the grid is then launched as its
+ * programmatic dependent, so the compression tiles run while the barrier
+ * still waits, and the step tiles wait for the barrier to finish.  With that
+ * flag next's buffers must already be complete before the barrier starts.
+ * Other flag bits: DFC_ERR_MODE.
  */
+#define DFC_FUSED_AFTER_BARRIER 1u
 DFC_API int dfc_zero_fused_step_ef(const void* const* comp_ptrs, void* const* param_ptrs,
                                    const void* comp_multicast, void* param_multicast,
                                    int32_t n_peers, int32_t rank, const DfcPeerSegment* segments,
                                    int32_t n_segments, const DfcHyper* hypers, int32_t n_hypers,
                                    int32_t mode, const float* device_grad_scale,
                                    const int32_t* error_flag, const DfcCompressRange* next,
-                                   int32_t ctas_per_sm, void* stream);
+                                   uint32_t flags, int32_t ctas_per_sm, void* stream);
 
 /*
  * The NVSwitch sum over every rank of numel bf16 values at a multicast

@@ -64,6 +64,7 @@ PEERSEG_DTYPE = np.dtype([("offset", "<i8"), ("numel", "<i8"), ("exp_avg", "<u8"
 COMPRESSRANGE_DTYPE = np.dtype([("grad", "<u8"), ("comp", "<u8"), ("resid", "<u8"),
                                 ("numel", "<i8")])
 MAX_PEERS = 8
+FUSED_AFTER_BARRIER = 1  # dfc_zero_fused_step_ef flag
 assert SEGMENT_DTYPE.itemsize == 48 and HYPER_DTYPE.itemsize == 48
 assert GRADREF_DTYPE.itemsize == 24 and GRADSTATS_DTYPE.itemsize == 24
 assert WORDRANGE_DTYPE.itemsize == 16 and PEERSEG_DTYPE.itemsize == 40
@@ -113,8 +114,8 @@ def _declare(h: ctypes.CDLL) -> None:
         "dfc_grad_stats_noalloc": ([P, I32, P, P], ctypes.c_int),
         "dfc_zero_fused_step": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, I32, P],
                                 ctypes.c_int),
-        "dfc_zero_fused_step_ef": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, P, I32, P],
-                                   ctypes.c_int),
+        "dfc_zero_fused_step_ef": ([P, P, P, P, I32, I32, P, I32, P, I32, I32, P, P, P,
+                                    ctypes.c_uint32, I32, P], ctypes.c_int),
         "dfc_peer_barrier": ([P, I32, I32, ctypes.c_uint32, P, I64, P], ctypes.c_int),
         "dfc_multicast_sum_bf16": ([P, P, I64, P], ctypes.c_int),
         "dfc_replay_encode": ([P, I64, P, P, I64, P, I64, P], ctypes.c_int),

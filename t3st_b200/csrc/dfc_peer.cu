@@ -227,13 +227,9 @@ __device__ __forceinline__ void scalar1(const ZeroBatch<MAXS, MAXH>& b, const Pe
 template <int MODE, int NP, bool NVLS, int MAXS, int MAXH>
 __global__ void __launch_bounds__(kThreads, 4)
     zero_step_kernel(const __grid_constant__ ZeroBatch<MAXS, MAXH> b) {
-  // A barrier before this kernel gave up: a peer may be stalled or gone, so
-  // neither its gradients nor its parameter copy may be touched.  The
-  // compression touches this rank's memory only and runs regardless.
-  const bool failed = b.error && *static_cast<const volatile int32_t*>(b.error) != 0;
-  if (failed && b.ctiles == 0) return;
   const int64_t ftiles = b.tile_base[b.n_segs];
   const int64_t total = ftiles + b.ctiles;
+  bool ready = false, failed = false;
   for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
     int64_t ft = u;
     if (b.ctiles) {
@@ -243,7 +239,21 @@ __global__ void __launch_bounds__(kThreads, 4)
         continue;
       }
     }
-    if (failed) continue;
+    if (!ready) {
+      // Launched as a programmatic dependent of the barrier (compression
+      // tiles then start while it waits): the step waits here for the
+      // barrier grid to finish.  Otherwise this returns at once.
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      // A barrier before this kernel gave up: a peer may be stalled or gone,
+      // so neither its gradients nor its parameter copy may be touched.  The
+      // compression touches this rank's memory only and runs regardless.
+      failed = b.error && *static_cast<const volatile int32_t*>(b.error) != 0;
+      ready = true;
+    }
+    if (failed) {
+      if (b.ctiles == 0) return;
+      continue;
+    }
     const int32_t t = static_cast<int32_t>(ft);
     int lo = 0, hi = b.n_segs;
     while (hi - lo > 1) {
@@ -268,32 +278,55 @@ __global__ void __launch_bounds__(kThreads, 4)
   }
 }
 
+// pdl: launched with programmatic stream serialization, so the grid may
+// start while the previous kernel on the stream runs, once that kernel allows
+// it (dfc_peer_barrier does, as it starts).
+template <typename Batch>
+cudaError_t launch_kernel(void (*kernel)(Batch), const Batch& b, int32_t grid, bool pdl,
+                          cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, b);
+}
+
 template <int MODE, int MAXS, int MAXH>
-void launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t grid, cudaStream_t st) {
-  if (b.comp_mc) {
-    zero_step_kernel<MODE, 0, true><<<grid, kThreads, 0, st>>>(b);
-    return;
-  }
+cudaError_t launch_np(const ZeroBatch<MAXS, MAXH>& b, int32_t grid, bool pdl, cudaStream_t st) {
+  if (b.comp_mc) return launch_kernel(zero_step_kernel<MODE, 0, true, MAXS, MAXH>, b, grid, pdl, st);
   switch (b.n_peers) {
-    case 2: zero_step_kernel<MODE, 2, false><<<grid, kThreads, 0, st>>>(b); break;
-    case 4: zero_step_kernel<MODE, 4, false><<<grid, kThreads, 0, st>>>(b); break;
-    case 8: zero_step_kernel<MODE, 8, false><<<grid, kThreads, 0, st>>>(b); break;
-    default: zero_step_kernel<MODE, 0, false><<<grid, kThreads, 0, st>>>(b); break;
+    case 2: return launch_kernel(zero_step_kernel<MODE, 2, false, MAXS, MAXH>, b, grid, pdl, st);
+    case 4: return launch_kernel(zero_step_kernel<MODE, 4, false, MAXS, MAXH>, b, grid, pdl, st);
+    case 8: return launch_kernel(zero_step_kernel<MODE, 8, false, MAXS, MAXH>, b, grid, pdl, st);
+    default: return launch_kernel(zero_step_kernel<MODE, 0, false, MAXS, MAXH>, b, grid, pdl, st);
   }
 }
 
 // One CTA per tile (ctas_per_sm <= 0), or at most ctas_per_sm CTAs per SM.
 template <int MAXS, int MAXH>
-int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, int32_t ctas_per_sm, cudaStream_t st) {
+int launch(const ZeroBatch<MAXS, MAXH>& b, int32_t mode, int32_t ctas_per_sm, bool pdl,
+           cudaStream_t st) {
   const int64_t tiles = static_cast<int64_t>(b.tile_base[b.n_segs]) + b.ctiles;
   if (tiles == 0) return DFC_OK;
   if (tiles > INT32_MAX) return DFC_ERR_SIZE;
   int32_t grid = static_cast<int32_t>(tiles);
   if (ctas_per_sm > 0) grid = static_cast<int32_t>(std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * ctas_per_sm));
+  cudaError_t e;
   switch (mode) {
-    case DFC_MODE_PLAIN: launch_np<DFC_MODE_PLAIN>(b, grid, st); break;
-    case DFC_MODE_SIGNFIBER: launch_np<DFC_MODE_SIGNFIBER>(b, grid, st); break;
-    default: launch_np<DFC_MODE_PACKED>(b, grid, st); break;
+    case DFC_MODE_PLAIN: e = launch_np<DFC_MODE_PLAIN>(b, grid, pdl, st); break;
+    case DFC_MODE_SIGNFIBER: e = launch_np<DFC_MODE_SIGNFIBER>(b, grid, pdl, st); break;
+    default: e = launch_np<DFC_MODE_PACKED>(b, grid, pdl, st); break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_cuda_error(e);
+    return DFC_ERR_CUDA;
   }
   return launch_status();
 }
@@ -342,6 +375,10 @@ struct BarrierArgs {
 };
 
 __global__ void peer_barrier_kernel(const __grid_constant__ BarrierArgs a) {
+  // A programmatic dependent launched after this kernel (the fused step with
+  // a compression in its grid) may start now; its step tiles still wait for
+  // this grid to finish (griddepcontrol.wait), its compression tiles do not.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int q = threadIdx.x;
   if (q >= a.n_peers) return;
   // an earlier barrier gave up: signal nobody, wait for nobody
@@ -375,12 +412,14 @@ int fused_step(const void* const* comp_ptrs, void* const* param_ptrs, const void
                void* param_multicast, int32_t n_peers, int32_t rank,
                const DfcPeerSegment* segments, int32_t n_segments, const DfcHyper* hypers,
                int32_t n_hypers, int32_t mode, const float* device_grad_scale,
-               const int32_t* error_flag, const DfcCompressRange* next, int32_t ctas_per_sm,
-               cudaStream_t st) {
+               const int32_t* error_flag, const DfcCompressRange* next, uint32_t flags,
+               int32_t ctas_per_sm, cudaStream_t st) {
   if (n_peers < 1 || n_peers > kMaxPeers || rank < 0 || rank >= n_peers) return DFC_ERR_SIZE;
   if (n_segments < 0 || n_hypers < 0) return DFC_ERR_SIZE;
   if (mode != DFC_MODE_PLAIN && mode != DFC_MODE_SIGNFIBER && mode != DFC_MODE_PACKED)
     return DFC_ERR_MODE;
+  if (flags & ~static_cast<uint32_t>(DFC_FUSED_AFTER_BARRIER)) return DFC_ERR_MODE;
+  bool pdl = (flags & DFC_FUSED_AFTER_BARRIER) != 0;  // the first launch only
   const bool compress = next && next->numel != 0;
   if (compress) {
     if (next->numel < 0 || next->numel % 4 != 0) return DFC_ERR_SIZE;
@@ -440,10 +479,11 @@ int fused_step(const void* const* comp_ptrs, void* const* param_ptrs, const void
     const bool need = local[s.hyper] < 0;
     if (b.n_segs == kMaxSegs || (need && static_cast<int>(used.size()) == kMaxHypers) ||
         b.tile_base[b.n_segs] > INT32_MAX / 2 - tiles) {
-      const int rc = launch(b, mode, ctas_per_sm, st);
+      const int rc = launch(b, mode, ctas_per_sm, pdl, st);
       if (rc != DFC_OK) return rc;
       reset();
       b.ctiles = 0;
+      pdl = false;
     }
     if (local[s.hyper] < 0) {
       local[s.hyper] = static_cast<int32_t>(used.size());
@@ -460,7 +500,7 @@ int fused_step(const void* const* comp_ptrs, void* const* param_ptrs, const void
     b.tile_base[b.n_segs + 1] = b.tile_base[b.n_segs] + tiles;
     ++b.n_segs;
   }
-  return (b.n_segs || b.ctiles) ? launch(b, mode, ctas_per_sm, st) : DFC_OK;
+  return (b.n_segs || b.ctiles) ? launch(b, mode, ctas_per_sm, pdl, st) : DFC_OK;
 }
 
 }  // namespace
@@ -474,7 +514,7 @@ extern "C" int dfc_zero_fused_step(const void* const* comp_ptrs, void* const* pa
                                    const int32_t* error_flag, int32_t ctas_per_sm, void* stream) {
   return dfc::fused_step(comp_ptrs, param_ptrs, comp_multicast, param_multicast, n_peers, rank,
                          segments, n_segments, hypers, n_hypers, mode, device_grad_scale,
-                         error_flag, nullptr, ctas_per_sm, static_cast<cudaStream_t>(stream));
+                         error_flag, nullptr, 0, ctas_per_sm, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dfc_zero_fused_step_ef(const void* const* comp_ptrs, void* const* param_ptrs,
@@ -483,11 +523,11 @@ extern "C" int dfc_zero_fused_step_ef(const void* const* comp_ptrs, void* const*
                                       const DfcPeerSegment* segments, int32_t n_segments,
                                       const DfcHyper* hypers, int32_t n_hypers, int32_t mode,
                                       const float* device_grad_scale, const int32_t* error_flag,
-                                      const DfcCompressRange* next, int32_t ctas_per_sm,
-                                      void* stream) {
+                                      const DfcCompressRange* next, uint32_t flags,
+                                      int32_t ctas_per_sm, void* stream) {
   return dfc::fused_step(comp_ptrs, param_ptrs, comp_multicast, param_multicast, n_peers, rank,
                          segments, n_segments, hypers, n_hypers, mode, device_grad_scale,
-                         error_flag, next, ctas_per_sm, static_cast<cudaStream_t>(stream));
+                         error_flag, next, flags, ctas_per_sm, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dfc_multicast_sum_bf16(const void* comp_multicast, float* out, int64_t numel,

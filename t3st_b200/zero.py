@@ -139,6 +139,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     b's fused kernel (dfc_zero_fused_step_ef) instead of in a
                     capped kernel on a second stream; one stream, one kernel
                     and one barrier per bucket
+    overlap_barrier with fuse_compression: launch each bucket's kernel as the
+                    programmatic dependent of the barrier before it, so its
+                    compression tiles run while the barrier waits (default on)
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3,
@@ -150,7 +153,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                  barrier_timeout_s: float = 30.0, backend=None,
                  fused_ctas_per_sm: int | None = None, compress_ctas_per_sm: int | None = None,
                  side_stream_priority: int = 0, overlap_buckets: bool = False,
-                 fuse_compression: bool = False):
+                 fuse_compression: bool = False, overlap_barrier: bool = True):
         if lr < 0 or eps < 0 or not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
             raise ValueError("invalid AdamW hyperparameters")
         if moment_format not in _FORMATS:
@@ -177,6 +180,7 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
         self.side_stream_priority = int(side_stream_priority)
         self.overlap_buckets = bool(overlap_buckets)
         self.fuse_compression = bool(fuse_compression)
+        self.overlap_barrier = bool(overlap_barrier)
         if self.fuse_compression and self.overlap_buckets:
             raise ValueError("fuse_compression runs every bucket on one stream; "
                              "overlap_buckets does not apply")
@@ -430,8 +434,9 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
     def _step_peer_fused_compression(self, rows, index):
         """One stream: C(0) alone (full grid); then for every bucket b a
         barrier (every rank's C(b) done) and one kernel that steps bucket b
-        and compresses bucket b+1 in the same grid; a last barrier ends the
-        step.  Error handling as in _step_peer (the compression tiles run
+        and compresses bucket b+1 in the same grid (with overlap_barrier its
+        compression tiles start while the barrier waits); a last barrier ends
+        the step.  Error handling as in _step_peer (the compression tiles run
         regardless: they touch only this rank's gradient buffers)."""
         self._check_peer_error()
         main = torch.cuda.current_stream(self.device)
@@ -451,7 +456,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     _lib.ptr(self._comp_arr), _lib.ptr(self._param_arr), self._comp_mc,
                     self._param_mc, self.world, self.rank, _lib.ptr(segs) if len(segs) else None,
                     len(segs), _lib.ptr(hyp), len(rows), self.mode, None,
-                    self.peer_error.data_ptr(), _lib.ptr(self._next_comp[b]), self.fused_ctas,
+                    self.peer_error.data_ptr(), _lib.ptr(self._next_comp[b]),
+                    _lib.FUSED_AFTER_BARRIER if self.overlap_barrier else 0, self.fused_ctas,
                     side.cuda_stream))
             self._barrier(side.cuda_stream)
             self._peer_error_host.copy_(self.peer_error, non_blocking=True)

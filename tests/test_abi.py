@@ -147,10 +147,10 @@ def test_other_entry_points_reject_bad_arguments():
     # compression range is checked before anything launches
     nxt = np.zeros(1, dtype=_lib.COMPRESSRANGE_DTYPE)
 
-    def fused_ef(rng, n_segs=1):
+    def fused_ef(rng, n_segs=1, flags=0):
         return lib.dfc_zero_fused_step_ef(comps, params, None, None, 2, 0, _lib.ptr(segs), n_segs,
                                           _lib.ptr(h), 1, _lib.MODE_PACKED, None, 0x70000,
-                                          None if rng is None else _lib.ptr(rng), 0, None)
+                                          None if rng is None else _lib.ptr(rng), flags, 0, None)
 
     nxt[0] = (0x80000, 0x90000, 0xA0000, 6)
     assert fused_ef(nxt) == _lib.DFC_ERR_SIZE       # not a whole number of quads
@@ -167,6 +167,7 @@ def test_other_entry_points_reject_bad_arguments():
     assert fused_ef(nxt) == _lib.DFC_ERR_HYPER      # the step's own checks still apply
     assert fused_ef(None) == _lib.DFC_ERR_HYPER
     segs[0]["hyper"] = 0
+    assert fused_ef(nxt, flags=2) == _lib.DFC_ERR_MODE  # unknown flag bit
     nxt[0] = (0, 0, 0, 0)                            # nothing to compress, no segments: no-op
     assert fused_ef(nxt, n_segs=0) == _lib.DFC_OK
     assert fused_ef(None, n_segs=0) == _lib.DFC_OK

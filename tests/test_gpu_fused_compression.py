@@ -12,7 +12,8 @@ against the oracle's compression.  Cases: one CTA per tile and a capped
 grid whose CTAs walk many tiles; more compression tiles than step tiles and
 fewer; ragged and misaligned segments (the per-element path); a set error
 flag (the step touches nothing, the compression still runs); no segments
-at all.
+at all; the launch as a barrier's programmatic dependent, behind a barrier
+that passes and one that gives up (a signal array nothing writes, 2 ms).
 """
 
 import ctypes
@@ -78,7 +79,10 @@ def _hypers():
                            hyper_row(5e-4, (0.8, 0.99), 1e-6, 0.0, 7, grad_scale=0.5)])
 
 
-def _run(cuda, step_sizes, n_comp, ctas, fused, error=False, seed=1):
+def _run(cuda, step_sizes, n_comp, ctas, fused, error=False, seed=1, flags=0, barrier=None):
+    """barrier: None, or "pass" / "give up": a dfc_peer_barrier of rank 0 of
+    two on the same stream first, whose other rank has already arrived /
+    never arrives (2 ms limit)."""
     from t3st_b200 import _lib
 
     lib = _lib.lib()
@@ -88,13 +92,21 @@ def _run(cuda, step_sizes, n_comp, ctas, fused, error=False, seed=1):
     segs = _segs(offsets, step_sizes, m, v)
     hyp = _hypers()
     flag = torch.full((1,), 2 if error else 0, dtype=torch.int32, device=cuda)
+    if barrier is not None:
+        mine = torch.zeros(2, dtype=torch.int32, device=cuda)
+        other = torch.zeros(2, dtype=torch.int32, device=cuda)
+        if barrier == "pass":
+            mine[1] = 1  # rank 1's epoch 1 is already in rank 0's array
+        torch.cuda.synchronize()
+        _lib.check("dfc_peer_barrier", lib.dfc_peer_barrier(
+            _ptrs(mine, other), 2, 0, 1, flag.data_ptr(), 2_000_000, stream))
     if fused:
         nxt = np.zeros(1, dtype=_lib.COMPRESSRANGE_DTYPE)
         nxt[0] = (cg.data_ptr(), cc.data_ptr(), cq.data_ptr(), n_comp)
         _lib.check("dfc_zero_fused_step_ef", lib.dfc_zero_fused_step_ef(
             _ptrs(*comps), _ptrs(*params), None, None, 2, 0,
             _lib.ptr(segs) if len(segs) else None, len(segs), _lib.ptr(hyp), 2,
-            _lib.MODE_PACKED, None, flag.data_ptr(), _lib.ptr(nxt), ctas, stream))
+            _lib.MODE_PACKED, None, flag.data_ptr(), _lib.ptr(nxt), flags, ctas, stream))
     else:
         if not error:
             _lib.check("dfc_zero_fused_step", lib.dfc_zero_fused_step(
@@ -156,6 +168,41 @@ def test_fused_compression_equals_the_two_calls(cuda, sizes, n_comp, ctas):
 def test_error_flag_skips_the_step_but_not_the_compression(cuda):
     sizes, n_comp = [6144 + 5, 2048], 2048 * 5 + 8
     got, p0, _ = _run(cuda, sizes, n_comp, 0, fused=True, error=True)
+    want, _, _ = _run(cuda, sizes, n_comp, 0, fused=False, error=True)  # compression only
+    np.testing.assert_array_equal(got["p0"].view(np.uint32), p0.view(np.uint32))
+    np.testing.assert_array_equal(got["p1"].view(np.uint32), p0.view(np.uint32))
+    _, _, _, m, v, _, _, _ = _case(cuda, 1, sizes, n_comp)
+    for k in range(len(sizes)):
+        np.testing.assert_array_equal(got[f"m{k}"], m[k].cpu().numpy())
+        np.testing.assert_array_equal(got[f"v{k}"], v[k].cpu().numpy())
+    np.testing.assert_array_equal(got["cc"], want["cc"])
+    np.testing.assert_array_equal(got["cq"], want["cq"])
+
+
+@pytest.mark.parametrize("sizes,n_comp,ctas", [CASES[0], CASES[2]])
+def test_launch_after_a_barrier_that_passes(cuda, sizes, n_comp, ctas):
+    """DFC_FUSED_AFTER_BARRIER behind a barrier whose other rank has arrived:
+    the grid starts as the barrier's programmatic dependent (compression
+    tiles at once, step tiles after the barrier); results equal the two
+    separate calls bit for bit."""
+    from t3st_b200 import _lib
+
+    got, _, _ = _run(cuda, sizes, n_comp, ctas, fused=True, flags=_lib.FUSED_AFTER_BARRIER,
+                     barrier="pass")
+    want, _, _ = _run(cuda, sizes, n_comp, ctas, fused=False)
+    for key in want:
+        np.testing.assert_array_equal(got[key], want[key], err_msg=key)
+
+
+def test_launch_after_a_barrier_that_gives_up(cuda):
+    """The same behind a barrier that gives up after 2 ms: the step tiles wait
+    for the barrier, see its flag and touch nothing; the compression is
+    done."""
+    from t3st_b200 import _lib
+
+    sizes, n_comp = [6144 + 5, 2048], 2048 * 5 + 8
+    got, p0, _ = _run(cuda, sizes, n_comp, 0, fused=True, flags=_lib.FUSED_AFTER_BARRIER,
+                      barrier="give up")
     want, _, _ = _run(cuda, sizes, n_comp, 0, fused=False, error=True)  # compression only
     np.testing.assert_array_equal(got["p0"].view(np.uint32), p0.view(np.uint32))
     np.testing.assert_array_equal(got["p1"].view(np.uint32), p0.view(np.uint32))
