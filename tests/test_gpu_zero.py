@@ -49,7 +49,7 @@ def _check_switch_sums(opt, red, world):
 
 
 def _run(rank, world, device, compress, transport="nccl", shapes=SHAPES, bucket=8192,
-         fused_ctas=None, overlap=False, fuse=False):
+         fused_ctas=None, overlap=False, fuse=None):
     from t3st_b200.zero import ShardedDFCAdamW
 
     torch.manual_seed(0)
@@ -253,13 +253,14 @@ def test_global_fiber_on_gpus(world):
 
 @pytest.mark.parametrize("transport", ["peer", "nvls"])
 def test_fused_kernel_walks_tiles_on_two_gpus(transport):
-    """One fused CTA per SM over a ~1M-element piece: every CTA of the
-    persistent grid steps several tiles; bit-exact as above."""
+    """One fused CTA per SM over ~1M-element pieces, with the compression in
+    its own capped kernel on the caller's stream: every CTA of the persistent
+    grid steps several tiles; bit-exact as above."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     if transport == "nvls" and not _multicast_ok():
         pytest.skip("no NVLink multicast on this node")
-    _spawn(2, transport, shapes=SHAPES_LARGE, bucket=1 << 22, fused_ctas=1)
+    _spawn(2, transport, shapes=SHAPES_LARGE, bucket=1 << 20, fused_ctas=1, fuse=False)
 
 
 @pytest.mark.parametrize("transport", ["peer", "nvls"])

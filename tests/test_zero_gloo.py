@@ -343,3 +343,4 @@ def test_fused_compression_excludes_bucket_overlap():
                         overlap_buckets=True)
     opt = ShardedDFCAdamW([torch.nn.Parameter(torch.zeros(8))], fuse_compression=True)
     assert opt.fuse_compression and opt.transport == "nccl"  # one rank: nothing to fuse into
+    assert not ShardedDFCAdamW([torch.nn.Parameter(torch.zeros(8))]).fuse_compression
