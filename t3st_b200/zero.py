@@ -61,11 +61,12 @@ DEFAULT_BUCKET = 1 << 26  # elements per bucket (256 MB of FP32 parameters)
 FUSED_CTAS_PER_SM = 0
 COMPRESS_CTAS_PER_SM = {2: 3}
 COMPRESS_CTAS_DEFAULT = 4
-# Rank counts where fuse_compression is the default: at 2 ranks over 2^30
-# elements it measured 5.32-5.34 ms per step against 5.59 for the capped
+# Rank counts where fuse_compression is the default: over 2^30 elements it
+# measured 5.32-5.34 ms per step at 2 ranks against 5.59 for the capped
 # compression on a second stream (the launch after the barrier made no
-# difference: 5.321 with, 5.326 without); not measured at 4 and 8 ranks.
-FUSE_COMPRESSION_WORLDS = (2,)
+# difference: 5.321 with, 5.326 without), and 7.37 against 7.47 at 4 ranks;
+# not measured at 8 ranks.
+FUSE_COMPRESSION_WORLDS = (2, 4)
 
 
 class CudaKernels:
@@ -143,8 +144,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     peer/nvls: compress bucket b+1 inside the grid of bucket
                     b's fused kernel (dfc_zero_fused_step_ef) instead of in a
                     capped kernel on a second stream; one stream, one kernel
-                    and one barrier per bucket (default: on at 2 ranks, where
-                    it was measured faster; off otherwise)
+                    and one barrier per bucket (default: on at 2 and 4
+                    ranks, where it was measured faster; off otherwise)
     overlap_barrier with fuse_compression: launch each bucket's kernel as the
                     programmatic dependent of the barrier before it, so its
                     compression tiles run while the barrier waits (default on)
