@@ -131,7 +131,8 @@ class ShardedDFCAdamW(torch.optim.Optimizer):
                     beyond where the node has NVLink multicast, else peer
     fused_ctas_per_sm, compress_ctas_per_sm
                     grid caps of the peer/nvls pipeline (defaults measured;
-                    compress_ctas_per_sm=0: the uncapped tile compression)
+                    compress_ctas_per_sm=0: the uncapped tile compression;
+                    with fuse_compression only the fused cap applies)
     side_stream_priority
                     CUDA priority of the stream that runs the barriers and the
                     fused kernel (lower is higher; PyTorch clamps to the
